@@ -1,0 +1,450 @@
+#!/usr/bin/env python
+"""Benchmark of the sm_100a AWQ W4A16 product (drop-in for kernels/awq_gemm.py).
+
+Headline metric: AWQ GEMM HBM TB/s at M=1 decode and TFLOP/s at
+M=2048 prefill, as fractions of the B200 roofline.
+
+One *step* = one decode token through the AWQ linears of the 28-layer Qwen2-7B stack
+at M=1, in the call shapes the reference uses (model/qwen2.py:81-83,104,156,176-186,196):
+fused qkv 3584x4608, o 3584x3584, fused gate+up 3584x37888, down 18944x3584.  That is
+112 launches and 3.39 GB of packed weights per step -- 27x the 126 MB L2, so every
+step streams from HBM (no flush needed).  Weights are random int4 in the AWQ layout
+with the benchmark's distributions (synthetic data; no checkpoint exists here).
+
+  value     algorithmic bytes of a step / device time of a step (CUDA events over K
+            CUDA-graph replays), TB/s, whole job (max over ranks)
+  e2e       the same bytes / time of a step made through the public drop-in
+            ``awq_gemm_forward`` with every call's x copied from pinned host memory
+            and every output copied back inside the timed region
+  roofline  decode kernel achieved GB/s vs MEASURED_PEAKS.json hbm_gbs
+  prefill   M=2048 gate+up and down through the tcgen05 kernel: TFLOP/s vs the
+            measured bf16 peak (fp16 and bf16 tensor rates are equal)
+  cpu_baseline  the reference's dequantize-then-fp32-matmul host path (oracle port,
+            torch on every host core) on one layer's 4 linears at M=1
+
+With torchrun (N > 1) every rank runs the tensor-parallel stack: qkv and gate+up
+column-sharded, o and down row-sharded with an NCCL all-reduce of the fp16 output
+(strong scaling: the token's total bytes are fixed).
+``--impl reference`` times the reference's own CPU path (oracle port) instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "qwen2-7b-triton_engine_b200"))
+sys.path.insert(0, str(REPO))
+
+HIDDEN, INTER, LAYERS, GS = 3584, 18944, 28, 128
+# (name, K, N) per layer, in call order
+STACK = [("qkv", HIDDEN, 4608), ("o", HIDDEN, HIDDEN), ("gate_up", HIDDEN, 2 * INTER),
+         ("down", INTER, HIDDEN)]
+SWEEP = {"q_o": (HIDDEN, HIDDEN), "k_v": (HIDDEN, 512), "qkv": (HIDDEN, 4608),
+         "gate_up": (HIDDEN, 2 * INTER), "down": (INTER, HIDDEN)}
+
+
+def alg_bytes(M, K, N, gs=GS):
+    """Algorithmic bytes of one call: packed weights + zeros + scales + x + out."""
+    return K * N // 2 + (K // gs) * (N // 8) * 4 + (K // gs) * N * 2 + 2 * M * K + 2 * M * N
+
+
+def load_peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["hbm_gbs"], d["bf16_tflops"], d.get("bf16_tflops_sustained"), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+# --------------------------------------------------------------------------- clocks --
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.rows = []
+        self.proc = None
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.rows.append(parts)
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.thread.join(timeout=5)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in self.rows:
+            for i, nm in enumerate(names):
+                if r[5 + i].lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(self.rows)}
+
+
+# ------------------------------------------------------------------------ helpers ----
+def make_layer_dev(torch, K, N, dev, gen):
+    qw = torch.randint(-2**31, 2**31, (K, N // 8), dtype=torch.int64, device=dev,
+                       generator=gen).to(torch.int32)
+    qz = torch.randint(-2**31, 2**31, (K // GS, N // 8), dtype=torch.int64, device=dev,
+                       generator=gen).to(torch.int32)
+    s = (torch.rand((K // GS, N), device=dev, generator=gen) * 0.018 + 0.002).half()
+    return qw, qz, s
+
+
+def shard_cols(t_qw, t_qz, t_s, rank, world):
+    """Column shard (split N) of one packed layer, in whole packed words."""
+    N = t_s.shape[1]
+    n = N // world
+    return (t_qw[:, rank * n // 8:(rank + 1) * n // 8].contiguous(),
+            t_qz[:, rank * n // 8:(rank + 1) * n // 8].contiguous(),
+            t_s[:, rank * n:(rank + 1) * n].contiguous())
+
+
+def cpu_baseline(torch, sample_seconds=12.0):
+    """Reference host path (oracle port) on one layer's 4 linears at M=1."""
+    from oracle import oracle as O
+    threads = O.cpu_threads()
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(11)
+    layers = []
+    for _, K, N in STACK:
+        qw = torch.randint(-2**31, 2**31, (K, N // 8), dtype=torch.int64, generator=g).to(torch.int32)
+        qz = torch.randint(-2**31, 2**31, (K // GS, N // 8), dtype=torch.int64, generator=g).to(torch.int32)
+        s = (torch.rand((K // GS, N), generator=g) * 0.018 + 0.002).half()
+        x = torch.randn((1, K), generator=g).half()
+        layers.append((x, qw, qz, s, alg_bytes(1, K, N)))
+    nbytes, secs, reps = 0, 0.0, 0
+    O.torch_awq_gemm_f32(*layers[0][:4])                      # warm-up
+    t0 = time.perf_counter()
+    while True:
+        for (x, qw, qz, s, b) in layers:
+            O.torch_awq_gemm_f32(x, qw, qz, s)
+            nbytes += b
+        reps += 1
+        secs = time.perf_counter() - t0
+        if secs >= sample_seconds or reps >= 50:
+            break
+    return {"value": nbytes / secs / 1e12, "unit": "TB/s", "cores": threads, "kind": "port",
+            "sample": f"{reps} x one Qwen2-7B layer (qkv, o, gate_up, down) at M=1: torch "
+                      f"dequant + fp32 matmul on {threads} host threads, {secs:.1f} s"}
+
+
+# ------------------------------------------------------------------------ our arm ----
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import awq_b200
+    from kernels import awq_gemm
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+    hbm_peak, tc_peak, tc_sust, peak_src = load_peaks()
+    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+
+    # ---- weights of the 28-layer stack (this rank's shards) -------------------------
+    calls = []          # (K_local, N_local, tensors, reduce?)
+    full_bytes = 0
+    for _ in range(LAYERS):
+        for name, K, N in STACK:
+            full_bytes += alg_bytes(1, K, N)
+            if world == 1:
+                calls.append((name, K, N, make_layer_dev(torch, K, N, dev, gen), False))
+            elif name in ("qkv", "gate_up"):            # column parallel
+                calls.append((name, K, N // world, make_layer_dev(torch, K, N // world, dev, gen),
+                               False))
+            else:                                       # row parallel + all-reduce
+                kl = K // world
+                kl -= kl % GS
+                if rank == world - 1:
+                    kl = K - kl * (world - 1)
+                calls.append((name, kl, N, make_layer_dev(torch, kl, N, dev, gen), True))
+    xs = {}
+    for name, K, N, _, _ in calls:
+        xs.setdefault(K, torch.randn((1, K), device=dev, generator=gen).half())
+    outs = [torch.empty((1, N), dtype=torch.float16, device=dev) for (_, _, N, _, _) in calls]
+    ws = awq_b200.workspace_for(dev, max(
+        awq_b200._lib.load().awq_gemm_workspace_bytes(1, N, K, GS) for (_, K, N, _, _) in calls))
+
+    lib = awq_b200._lib.load()
+    stream = torch.cuda.Stream(device=dev)
+
+    def step():
+        h = torch.cuda.current_stream(dev).cuda_stream
+        for i, (name, K, N, (qw, qz, s), red) in enumerate(calls):
+            x = xs[K]
+            rc = lib.awq_gemm_f16(x.data_ptr(), K, qw.data_ptr(), qz.data_ptr(), s.data_ptr(),
+                                  outs[i].data_ptr(), N, 1, N, K, GS, ws.data_ptr(), ws.numel(),
+                                  h)
+            if rc:
+                awq_b200._lib.check(rc)
+            if red:
+                dist.all_reduce(outs[i])
+
+    # warm-up (eager), then capture one step into a CUDA graph
+    with torch.cuda.stream(stream):
+        for _ in range(max(1, args.warmup)):
+            step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+
+    # ---- timed region: K graph replays ----------------------------------------------
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            ev1.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = full_bytes / (ms * 1e-3) / 1e12
+    del graph
+    torch.cuda.synchronize()
+
+    result = None
+    if rank == 0:
+        local_bytes = sum(alg_bytes(1, K, N) for (_, K, N, _, _) in calls)
+        achieved = local_bytes / (ms * 1e-3) / 1e9
+        result = {
+            "metric": "AWQ GEMM HBM TB/s (M=1 decode) & TFLOPS (M=2048 prefill), % of B200 roofline",
+            "value": round(value, 4), "unit": "TB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
+            "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (seeded random int4 AWQ weights, x ~ N(0,1); no checkpoint)",
+            "config": {"workload": "decode M=1 through the AWQ linears of the 28-layer Qwen2-7B "
+                                   "stack (qkv 3584x4608, o 3584x3584, gate_up 3584x37888, down "
+                                   "18944x3584 per layer; 112 launches, CUDA-graph replay)",
+                       "bytes_per_step": full_bytes, "group_size": GS,
+                       "l2": "working set 3.39 GB > 126 MB L2 (no flush needed)",
+                       "parallelism": f"tp{world}" if world > 1 else "single"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak,
+                         "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
+                         "peak_source": peak_src, "traffic": None,
+                         "kernel": "awq::gemv_kernel (decode, mma.sync split-K)"},
+            "gpu_launches": args.steps * len(calls),
+        }
+        result["clocks"] = clk.summary()
+
+    # ---- end to end through the public drop-in, host buffers ------------------------
+    if world == 1:
+        hx = [torch.randn((1, K)).half().pin_memory() for (_, K, _, _, _) in calls]
+        hout = [torch.empty((1, N), dtype=torch.float16).pin_memory() for (_, _, N, _, _) in calls]
+        dx = [torch.empty((1, K), dtype=torch.float16, device=dev) for (_, K, _, _, _) in calls]
+
+        def e2e_step():
+            for i, (name, K, N, (qw, qz, s), _) in enumerate(calls):
+                dx[i].copy_(hx[i], non_blocking=True)
+                y = awq_gemm.awq_gemm_forward(dx[i], qw, qz, s, GS)
+                hout[i].copy_(y, non_blocking=True)
+            torch.cuda.synchronize()
+        for _ in range(max(1, args.warmup)):
+            e2e_step()
+        e2e_steps = max(3, min(args.steps, 20))
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            e2e_step()
+        e2e_ms = (time.perf_counter() - t0) * 1e3 / e2e_steps
+        result["e2e"] = {"value": round(full_bytes / (e2e_ms * 1e-3) / 1e12, 4), "unit": "TB/s",
+                         "ms_per_step": round(e2e_ms, 4),
+                         "h2d_bytes_per_step": sum(2 * K for (_, K, _, _, _) in calls),
+                         "d2h_bytes_per_step": sum(2 * N for (_, _, N, _, _) in calls),
+                         "api": "kernels.awq_gemm.awq_gemm_forward (eager, 112 calls)"}
+        result["gpu_launches"] += 0
+        result["prefill"] = prefill_bench(torch, awq_b200, dev, tc_peak, peak_src, args)
+        result["sweep"] = decode_sweep(torch, lib, awq_b200, dev, hbm_peak)
+        result["cpu_baseline"] = cpu_baseline(torch, args.cpu_seconds)
+    if world > 1:
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result))
+
+
+def prefill_bench(torch, awq_b200, dev, tc_peak, peak_src, args):
+    """M=2048 gate+up and down through the tcgen05 kernel (or the decode fallback)."""
+    M = 2048
+    gen = torch.Generator(device=dev).manual_seed(77)
+    res = {"metric": "AWQ GEMM TFLOP/s (M=2048 prefill)", "unit": "TFLOP/s"}
+    tot_flops, tot_ms = 0, 0.0
+    for name, K, N in (("gate_up", HIDDEN, 2 * INTER), ("down", INTER, HIDDEN)):
+        qw, qz, s = make_layer_dev(torch, K, N, dev, gen)
+        x = torch.randn((M, K), device=dev, generator=gen).half()
+        out = torch.empty((M, N), dtype=torch.float16, device=dev)
+        tc = awq_b200.tc_supported(x, qw, qz, s, GS)
+        path = awq_b200.AWQ_PATH_TC if tc else awq_b200.AWQ_PATH_DECODE
+        flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+        for _ in range(3):
+            awq_b200.gemm(x, qw, qz, s, GS, path=path, out=out)
+        reps = 5
+        times = []
+        for _ in range(reps):
+            flush.zero_()                      # evict the 126 MB L2 between launches
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            awq_b200.gemm(x, qw, qz, s, GS, path=path, out=out)
+            e1.record()
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1))
+        ms = statistics.median(times)
+        flops = 2 * M * K * N
+        tf = flops / (ms * 1e-3) / 1e12
+        res[name] = {"K": K, "N": N, "ms": round(ms, 4), "tflops": round(tf, 1),
+                     "frac": round(tf / tc_peak, 4),
+                     "kernel": "tcgen05" if tc else "decode-fallback"}
+        tot_flops += flops
+        tot_ms += ms
+        del qw, qz, s, x, out, flush
+    tf = tot_flops / (tot_ms * 1e-3) / 1e12
+    res["value"] = round(tf, 1)
+    res["roofline"] = {"bound": "tensor", "achieved": round(tf, 1), "peak": tc_peak,
+                       "unit": "TFLOP/s", "frac": round(tf / tc_peak, 4),
+                       "peak_source": f"{peak_src} bf16 burst (fp16 rate is equal)"}
+    return res
+
+
+def decode_sweep(torch, lib, awq_b200, dev, hbm_peak):
+    """Per-shape decode GB/s at M in {1,4,16}, weights rotated over a > 2x L2 pool."""
+    gen = torch.Generator(device=dev).manual_seed(99)
+    out = {}
+    for name, (K, N) in SWEEP.items():
+        per = alg_bytes(1, K, N)
+        copies = max(2, int((300 << 20) // per) + 1)           # pool > 2x L2
+        pool = [make_layer_dev(torch, K, N, dev, gen) for _ in range(copies)]
+        for M in (1, 4, 16):
+            x = torch.randn((M, K), device=dev, generator=gen).half()
+            o = torch.empty((M, N), dtype=torch.float16, device=dev)
+            for w in pool[:2]:
+                awq_b200.gemm(x, *w, GS, out=o)
+            reps = 200
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for r in range(copies):
+                    awq_b200.gemm(x, *pool[r], GS, out=o)
+            g.replay()
+            torch.cuda.synchronize()
+            nrep = max(1, reps // copies)
+            e0.record()
+            for _ in range(nrep):
+                g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / (nrep * copies)
+            gbs = alg_bytes(M, K, N) / (us * 1e-6) / 1e9
+            out[f"{name}_M{M}"] = {"us": round(us, 2), "GBps": round(gbs, 1),
+                                   "frac": round(gbs / hbm_peak, 3)}
+            del g
+        del pool
+    return out
+
+
+# ------------------------------------------------------------------ reference arm ----
+def run_reference(args):
+    """The reference's own CPU implementation of the path (dequantize, then fp32
+    matmul on the host), on this arm's metric and config, rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    import torch
+    cb = cpu_baseline(torch, sample_seconds=max(2.0, args.cpu_seconds / max(1, args.steps)))
+    value = cb["value"]
+    per_layer = sum(alg_bytes(1, K, N) for (_, K, N) in STACK)
+    ms = per_layer * LAYERS / (value * 1e12) * 1e3
+    print(json.dumps({
+        "impl": "reference",
+        "metric": "AWQ GEMM HBM TB/s (M=1 decode) & TFLOPS (M=2048 prefill), % of B200 roofline",
+        "value": round(value, 6), "unit": "TB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "decode M=1 through the AWQ linears of the 28-layer Qwen2-7B "
+                               "stack (timed on a bounded sample: one layer's 4 linears)",
+                   "path": "reference dequantize-then-matmul on host cores (oracle port of "
+                           "test/compare_benchmark.py:72-95 with an fp32 matmul)"},
+        "cpu_baseline": cb,
+        "e2e": {"value": round(value, 6), "unit": "TB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,109 @@
+/*
+ * awq_b200.h -- C ABI of the B200 (sm_100a) AWQ W4A16 library, libawq_b200.so.
+ *
+ * Drop-in boundary for songqiuyu/Qwen2-7B-Triton_Engine's AWQ matrix product.
+ * Every entry point takes plain pointers and sizes; device pointers are owned by
+ * the caller and never freed here.  Streams are passed as `void*` holding a
+ * cudaStream_t (NULL = the legacy default stream).  No entry point allocates
+ * device memory, synchronizes the device, or throws; each returns AWQ_OK (0) or
+ * a negative AWQ_ERR_* code, and awq_last_error() gives a message for the
+ * calling thread.
+ *
+ * Packed layout (model/qwen2.py:34-36, kernels/awq_gemm.py:36-38):
+ *   qweight int32 [K, N/8]   row-major; element n of row k is the nibble at bit
+ *                            4 * order[n % 8] of word n / 8, order = 0,4,1,5,2,6,3,7
+ *   qzeros  int32 [K/gs, N/8]
+ *   scales  fp16  [K/gs, N]
+ *   W[k, n] = fp16(w - z) * scale in fp16 (kernels/awq_gemm.py:59)
+ * Requirements: N % 8 == 0, group_size % 8 == 0, K % group_size == 0; qweight,
+ * qzeros, scales and out 16-byte aligned and densely packed (row stride = width);
+ * x rows of length K with stride ldx >= K (elements), 2-byte aligned.
+ */
+#ifndef AWQ_B200_H_
+#define AWQ_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define AWQ_API __attribute__((visibility("default")))
+#else
+#define AWQ_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define AWQ_OK 0
+#define AWQ_ERR_INVALID_ARG (-1)   /* null pointer, bad shape, bad alignment       */
+#define AWQ_ERR_UNSUPPORTED (-2)   /* valid input this build cannot run (e.g. path) */
+#define AWQ_ERR_CUDA (-3)          /* a CUDA runtime call failed                    */
+#define AWQ_ERR_WORKSPACE (-4)     /* workspace missing or too small                */
+#define AWQ_ERR_DEVICE (-5)        /* a kernel reported an error (awq_device_status) */
+
+/* Kernel choice for awq_gemm_f16_ex. */
+#define AWQ_PATH_AUTO 0   /* M <= 16: decode kernel; larger M: tcgen05 GEMM when the shape allows */
+#define AWQ_PATH_DECODE 1 /* mma.sync split-K streaming kernel, any M (16-token chunks)          */
+#define AWQ_PATH_TC 2     /* tcgen05/TMEM prefill GEMM; AWQ_ERR_UNSUPPORTED if shape disallows   */
+
+/* Library version: major * 10000 + minor * 100 + patch. */
+AWQ_API int awq_version(void);
+
+/* Message describing the last error returned on this thread ("" if none). */
+AWQ_API const char* awq_last_error(void);
+
+/*
+ * Bit-exact dequantization: out fp16 [K, N] = W.
+ * Replaces _dequant_to_fp16 / _dequant_awq_kernel (kernels/awq_gemm.py:14-87).
+ */
+AWQ_API int awq_dequant_f16(const int32_t* qweight, const int32_t* qzeros, const void* scales, void* out,
+                    int64_t K, int64_t N, int64_t group_size, void* stream);
+
+/*
+ * Bytes of workspace awq_gemm_f16 / awq_gemm_f16_ex need for this shape on the
+ * current device (0 is a valid answer).  The workspace holds split-K partial sums
+ * and arrival counters.  It must be zero-filled once before its first use
+ * (awq_workspace_init); every completed call leaves the counters at zero again.
+ * Calls that run concurrently (different streams) need different workspaces.
+ * No counterpart in the reference (its M<=4 path keeps a global K*N fp16 buffer,
+ * kernels/awq_gemm.py:234,255-262).
+ */
+AWQ_API size_t awq_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t group_size);
+
+/* Zero-fill a workspace on `stream` (cudaMemsetAsync). */
+AWQ_API int awq_workspace_init(void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * out fp16 [M, N] (row stride ldo) = x fp16 [M, K] (row stride ldx) @ W, fp32
+ * accumulation.  Replaces awq_gemm_forward (kernels/awq_gemm.py:237-284) after its
+ * reshape of x to [M, K]: M <= 16 runs the decode kernel, larger M the tcgen05
+ * GEMM when the shape allows it, else the decode kernel over 16-token chunks.
+ */
+AWQ_API int awq_gemm_f16(const void* x, int64_t ldx, const int32_t* qweight, const int32_t* qzeros,
+                 const void* scales, void* out, int64_t ldo, int64_t M, int64_t N, int64_t K,
+                 int64_t group_size, void* workspace, size_t workspace_bytes, void* stream);
+
+/* awq_gemm_f16 with an explicit kernel choice (AWQ_PATH_*), for tests and benchmarks. */
+AWQ_API int awq_gemm_f16_ex(const void* x, int64_t ldx, const int32_t* qweight, const int32_t* qzeros,
+                    const void* scales, void* out, int64_t ldo, int64_t M, int64_t N, int64_t K,
+                    int64_t group_size, void* workspace, size_t workspace_bytes, void* stream,
+                    int path);
+
+/* 1 if AWQ_PATH_TC can run this shape with these pointers, else 0. */
+AWQ_API int awq_tc_supported(const void* x, int64_t ldx, const int32_t* qweight, const int32_t* qzeros,
+                     const void* scales, int64_t M, int64_t N, int64_t K, int64_t group_size);
+
+/*
+ * Synchronizes `stream`, then reads and clears the current device's kernel status
+ * word.  Returns AWQ_OK, or AWQ_ERR_DEVICE with the status bits in *status_out
+ * (1 = a bounded barrier wait timed out, 2 = a kernel rejected its parameters).
+ * No counterpart in the reference.
+ */
+AWQ_API int awq_device_status(void* stream, int* status_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AWQ_B200_H_ */

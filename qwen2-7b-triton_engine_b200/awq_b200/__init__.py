@@ -1,0 +1,193 @@
+"""awq_b200 -- host side of the sm_100a AWQ W4A16 library.
+
+Thin PyTorch-facing layer over libawq_b200.so: tensor checks, device/stream
+selection and the per-(device, stream) split-K workspace.  All compute happens in
+the CUDA library; nothing here has a CPU fallback.
+
+Public functions
+  dequant(qweight, qzeros, scales, group_size)      -> fp16 [K, N]   (bit-exact W)
+  gemm(x2d, qweight, qzeros, scales, group_size, path) -> fp16 [M, N]
+  device_status(stream)                              -> status bits of the kernels
+The reference-facing drop-in, ``kernels.awq_gemm.awq_gemm_forward``, is built on
+``gemm``.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+
+import torch
+
+from . import _lib
+from ._lib import (AWQ_PATH_AUTO, AWQ_PATH_DECODE, AWQ_PATH_TC, AwqError,  # noqa: F401
+                   LIB_PATH)
+
+__all__ = ["dequant", "gemm", "device_status", "workspace_for", "AwqError",
+           "AWQ_PATH_AUTO", "AWQ_PATH_DECODE", "AWQ_PATH_TC", "LIB_PATH"]
+
+_ws_lock = threading.Lock()
+_workspaces: dict = {}
+
+
+def _require_cuda(t: torch.Tensor, name: str) -> None:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if t.device.type != "cuda":
+        raise ValueError(f"{name} is on {t.device}; the AWQ kernels run on CUDA only "
+                         "(no CPU fallback)")
+
+
+def _dense16(t: torch.Tensor) -> torch.Tensor:
+    """Contiguous and 16-byte aligned (copies only when needed)."""
+    if not t.is_contiguous():
+        t = t.contiguous()
+    if t.data_ptr() % 16:
+        t = t.clone()
+    return t
+
+
+def check_weights(qweight, qzeros, scales, group_size):
+    """Validate the packed layout; returns (K, N).  Mirrors the shapes that
+    LinearAWQ registers (model/qwen2.py:34-36); N comes from scales.shape[1] as in
+    awq_gemm_forward (kernels/awq_gemm.py:247)."""
+    for t, name in ((qweight, "qweight"), (qzeros, "qzeros"), (scales, "scales")):
+        _require_cuda(t, name)
+        if t.dim() != 2:
+            raise ValueError(f"{name} must be 2-D, got shape {tuple(t.shape)}")
+    if qweight.dtype != torch.int32 or qzeros.dtype != torch.int32:
+        raise TypeError("qweight and qzeros must be int32")
+    if scales.dtype != torch.float16:
+        raise TypeError("scales must be float16")
+    if not (qweight.device == qzeros.device == scales.device):
+        raise ValueError("qweight, qzeros and scales must be on one device")
+    group_size = int(group_size)
+    K = qweight.shape[0]
+    N = scales.shape[1]
+    if qweight.shape[1] * 8 != N:
+        raise ValueError(f"scales.shape[1]={N} but qweight packs {qweight.shape[1] * 8} columns")
+    if group_size <= 0 or K % group_size:
+        raise ValueError(f"K={K} is not a multiple of group_size={group_size}")
+    G = K // group_size
+    if tuple(qzeros.shape) != (G, N // 8) or tuple(scales.shape) != (G, N):
+        raise ValueError(f"qzeros {tuple(qzeros.shape)} / scales {tuple(scales.shape)} do not "
+                         f"match [K/group_size={G}, N/8={N // 8}] / [{G}, {N}]")
+    return K, N
+
+
+def _stream_handle(device: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+class _DeviceGuard:
+    """Make `device` current for the ctypes call only when it is not already."""
+
+    def __init__(self, device: torch.device):
+        self.idx = device.index if device.index is not None else torch.cuda.current_device()
+        self.prev = None
+
+    def __enter__(self):
+        cur = torch.cuda.current_device()
+        if cur != self.idx:
+            self.prev = cur
+            torch.cuda.set_device(self.idx)
+
+    def __exit__(self, *exc):
+        if self.prev is not None:
+            torch.cuda.set_device(self.prev)
+
+
+def workspace_for(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Zero-initialised split-K workspace for (device, current stream), grown on demand.
+
+    The kernels leave its arrival counters at zero after every call, so it is
+    zeroed once per allocation only.  One workspace per stream keeps concurrent
+    streams from sharing counters.
+    """
+    stream = torch.cuda.current_stream(device)
+    key = (device.index, stream.cuda_stream)
+    with _ws_lock:
+        ws = _workspaces.get(key)
+        if ws is None or ws.numel() < nbytes:
+            size = max(nbytes, 1 << 20)
+            ws = torch.zeros(size, dtype=torch.uint8, device=device)
+            _workspaces[key] = ws
+        return ws
+
+
+def dequant(qweight: torch.Tensor, qzeros: torch.Tensor, scales: torch.Tensor,
+            group_size: int = 128, out: torch.Tensor | None = None) -> torch.Tensor:
+    """fp16 [K, N] dequantized weights, bit-identical to the reference's
+    _dequant_to_fp16 (kernels/awq_gemm.py:66-87)."""
+    K, N = check_weights(qweight, qzeros, scales, group_size)
+    qweight, qzeros, scales = _dense16(qweight), _dense16(qzeros), _dense16(scales)
+    dev = qweight.device
+    if out is None:
+        out = torch.empty((K, N), dtype=torch.float16, device=dev)
+    else:
+        _require_cuda(out, "out")
+        if out.dtype != torch.float16 or tuple(out.shape) != (K, N) or not out.is_contiguous() \
+                or out.data_ptr() % 16:
+            raise ValueError("out must be a contiguous, 16-byte aligned fp16 [K, N] tensor")
+    lib = _lib.load()
+    with _DeviceGuard(dev):
+        _lib.check(lib.awq_dequant_f16(qweight.data_ptr(), qzeros.data_ptr(), scales.data_ptr(),
+                                       out.data_ptr(), K, N, int(group_size),
+                                       _stream_handle(dev)))
+    return out
+
+
+def gemm(x2d: torch.Tensor, qweight: torch.Tensor, qzeros: torch.Tensor, scales: torch.Tensor,
+         group_size: int = 128, path: int = AWQ_PATH_AUTO,
+         out: torch.Tensor | None = None) -> torch.Tensor:
+    """fp16 [M, N] = x2d fp16 [M, K] @ W with fp32 accumulation, on the current stream."""
+    K, N = check_weights(qweight, qzeros, scales, group_size)
+    _require_cuda(x2d, "x")
+    if x2d.dtype != torch.float16:
+        raise TypeError(f"x must be float16, got {x2d.dtype}")
+    if x2d.dim() != 2 or x2d.shape[1] != K:
+        raise ValueError(f"x must be [M, K={K}], got {tuple(x2d.shape)}")
+    if x2d.device != qweight.device:
+        raise ValueError("x and the weights must be on one device")
+    M = x2d.shape[0]
+    dev = x2d.device
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float16, device=dev)
+    if M == 0:
+        return out
+    qweight, qzeros, scales = _dense16(qweight), _dense16(qzeros), _dense16(scales)
+    if x2d.stride(1) != 1 or x2d.data_ptr() % 16 or (x2d.stride(0) * 2) % 16:
+        x2d = x2d.contiguous()
+        if x2d.data_ptr() % 16:
+            x2d = x2d.clone()
+    lib = _lib.load()
+    with _DeviceGuard(dev):
+        need = lib.awq_gemm_workspace_bytes(M, N, K, int(group_size))
+        ws = workspace_for(dev, need) if need else None
+        _lib.check(lib.awq_gemm_f16_ex(
+            x2d.data_ptr(), x2d.stride(0), qweight.data_ptr(), qzeros.data_ptr(),
+            scales.data_ptr(), out.data_ptr(), out.stride(0), M, N, K, int(group_size),
+            ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
+            _stream_handle(dev), int(path)))
+    return out
+
+
+def tc_supported(x2d, qweight, qzeros, scales, group_size: int = 128) -> bool:
+    """Whether the tcgen05 prefill kernel accepts this shape and these pointers."""
+    lib = _lib.load()
+    K, N = qweight.shape[0], scales.shape[1]
+    return bool(lib.awq_tc_supported(x2d.data_ptr(), x2d.stride(0), qweight.data_ptr(),
+                                     qzeros.data_ptr(), scales.data_ptr(), x2d.shape[0], N, K,
+                                     int(group_size)))
+
+
+def device_status(device=None) -> int:
+    """Synchronise the current stream and return (and clear) the kernels' status bits."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None \
+        else torch.device(device)
+    lib = _lib.load()
+    st = ctypes.c_int(0)
+    with _DeviceGuard(dev):
+        rc = lib.awq_device_status(_stream_handle(dev), ctypes.byref(st))
+    if rc not in (_lib.AWQ_OK, _lib.AWQ_ERR_DEVICE):
+        _lib.check(rc)
+    return st.value

@@ -1,0 +1,218 @@
+// awq_capi.cu -- extern "C" entry points of libawq_b200.so (declared in include/awq_b200.h).
+//
+// Validation, kernel choice and workspace accounting for the AWQ W4A16 product.  The
+// Python drop-in (kernels/awq_gemm.py in this package) calls these through ctypes; a
+// C/C++ host can link them directly.  Mirrors the dispatch of awq_gemm_forward
+// (songqiuyu/Qwen2-7B-Triton_Engine kernels/awq_gemm.py:237-284) with the decode /
+// prefill split moved from M <= 4 to M <= 16 and both branches replaced by sm_100a
+// kernels that read the packed weights directly.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/awq_b200.h"
+#include "awq_internal.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int fail_cuda(cudaError_t e, const char* what) {
+  return fail(AWQ_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+__device__ int g_device_status;   // one per device; kernels OR their error bits in
+
+constexpr int kMaxDevices = 64;
+struct DeviceInfo {
+  int num_sms = 0;
+  int* status = nullptr;
+  bool ready = false;
+};
+DeviceInfo g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+int device_info(DeviceInfo** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail_cuda(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(AWQ_ERR_UNSUPPORTED, "device %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (!d.ready) {
+    int sms = 0, major = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return fail_cuda(e, "cudaDeviceGetAttribute");
+    e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    if (e != cudaSuccess) return fail_cuda(e, "cudaDeviceGetAttribute");
+    if (major != 10)
+      return fail(AWQ_ERR_UNSUPPORTED, "device %d has compute capability %d.x; this library is built for sm_100a",
+                  dev, major);
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_device_status);
+    if (e != cudaSuccess) return fail_cuda(e, "cudaGetSymbolAddress(status)");
+    d.num_sms = sms;
+    d.status = static_cast<int*>(p);
+    d.ready = true;
+  }
+  *out = &d;
+  return AWQ_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+int check_weights(const int32_t* qweight, const int32_t* qzeros, const void* scales, int64_t K,
+                  int64_t N, int64_t group_size) {
+  if (!qweight || !qzeros || !scales) return fail(AWQ_ERR_INVALID_ARG, "null weight pointer");
+  if (K <= 0 || N <= 0) return fail(AWQ_ERR_INVALID_ARG, "K=%lld N=%lld must be positive", (long long)K, (long long)N);
+  if (N % 8) return fail(AWQ_ERR_INVALID_ARG, "N=%lld is not a multiple of 8", (long long)N);
+  if (group_size <= 0 || group_size % 8)
+    return fail(AWQ_ERR_INVALID_ARG, "group_size=%lld must be a positive multiple of 8", (long long)group_size);
+  if (K % group_size)
+    return fail(AWQ_ERR_INVALID_ARG, "K=%lld is not a multiple of group_size=%lld", (long long)K, (long long)group_size);
+  if (K > (int64_t)1 << 30 || N > (int64_t)1 << 30)
+    return fail(AWQ_ERR_INVALID_ARG, "K or N above 2^30");
+  if (!aligned16(qweight) || !aligned16(qzeros) || !aligned16(scales))
+    return fail(AWQ_ERR_INVALID_ARG, "qweight, qzeros and scales must be 16-byte aligned");
+  return AWQ_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int awq_version(void) { return 100; }
+
+const char* awq_last_error(void) { return g_last_error.c_str(); }
+
+int awq_dequant_f16(const int32_t* qweight, const int32_t* qzeros, const void* scales, void* out,
+                    int64_t K, int64_t N, int64_t group_size, void* stream) {
+  int rc = check_weights(qweight, qzeros, scales, K, N, group_size);
+  if (rc) return rc;
+  if (!out || !aligned16(out)) return fail(AWQ_ERR_INVALID_ARG, "out must be a 16-byte aligned pointer");
+  DeviceInfo* d = nullptr;
+  if ((rc = device_info(&d))) return rc;
+  cudaError_t e = awq::launch_dequant(qweight, qzeros, scales, out, K, N, group_size, d->num_sms,
+                                      static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail_cuda(e, "dequant launch");
+  return AWQ_OK;
+}
+
+size_t awq_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t group_size) {
+  DeviceInfo* d = nullptr;
+  if (device_info(&d)) return 0;
+  awq::GemvPlan plan;
+  if (!awq::plan_gemv(M, N, K, group_size, d->num_sms, true, &plan)) return 0;
+  size_t a = awq::gemv_workspace_bytes(plan);
+  // the unaligned (scalar-load) plan has the same grid, so the same size
+  return a;
+}
+
+int awq_workspace_init(void* workspace, size_t workspace_bytes, void* stream) {
+  if (workspace_bytes == 0) return AWQ_OK;
+  if (!workspace) return fail(AWQ_ERR_INVALID_ARG, "null workspace");
+  cudaError_t e = cudaMemsetAsync(workspace, 0, workspace_bytes, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail_cuda(e, "cudaMemsetAsync(workspace)");
+  return AWQ_OK;
+}
+
+int awq_tc_supported(const void* x, int64_t ldx, const int32_t* qweight, const int32_t* qzeros,
+                     const void* scales, int64_t M, int64_t N, int64_t K, int64_t group_size) {
+  return awq::tc_supported(x, ldx, qweight, qzeros, scales, M, N, K, group_size) ? 1 : 0;
+}
+
+int awq_gemm_f16_ex(const void* x, int64_t ldx, const int32_t* qweight, const int32_t* qzeros,
+                    const void* scales, void* out, int64_t ldo, int64_t M, int64_t N, int64_t K,
+                    int64_t group_size, void* workspace, size_t workspace_bytes, void* stream,
+                    int path) {
+  int rc = check_weights(qweight, qzeros, scales, K, N, group_size);
+  if (rc) return rc;
+  if (!x || !out) return fail(AWQ_ERR_INVALID_ARG, "null x or out");
+  if (M <= 0 || M > (int64_t)1 << 30) return fail(AWQ_ERR_INVALID_ARG, "M=%lld out of range", (long long)M);
+  if (ldx < K || ldo < N) return fail(AWQ_ERR_INVALID_ARG, "ldx < K or ldo < N");
+  if ((reinterpret_cast<uintptr_t>(x) & 1) || (reinterpret_cast<uintptr_t>(out) & 1))
+    return fail(AWQ_ERR_INVALID_ARG, "x and out must be 2-byte aligned");
+  if (path != AWQ_PATH_AUTO && path != AWQ_PATH_DECODE && path != AWQ_PATH_TC)
+    return fail(AWQ_ERR_INVALID_ARG, "unknown path %d", path);
+  DeviceInfo* d = nullptr;
+  if ((rc = device_info(&d))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  bool use_tc = false;
+  if (path == AWQ_PATH_TC) {
+    if (!awq::tc_supported(x, ldx, qweight, qzeros, scales, M, N, K, group_size))
+      return fail(AWQ_ERR_UNSUPPORTED, "tcgen05 path cannot run M=%lld N=%lld K=%lld gs=%lld with these pointers",
+                  (long long)M, (long long)N, (long long)K, (long long)group_size);
+    use_tc = true;
+  } else if (path == AWQ_PATH_AUTO) {
+    use_tc = M > 16 && awq::tc_supported(x, ldx, qweight, qzeros, scales, M, N, K, group_size);
+  }
+
+  if (use_tc) {
+    const char* why = nullptr;
+    cudaError_t e = awq::launch_gemm_tc(x, ldx, qweight, qzeros, scales, out, ldo, (int)M, (int)N,
+                                        (int)K, (int)group_size, d->num_sms, d->status, st, &why);
+    if (why) return fail(AWQ_ERR_UNSUPPORTED, "tcgen05 path: %s", why);
+    if (e != cudaSuccess) return fail_cuda(e, "tcgen05 GEMM launch");
+    return AWQ_OK;
+  }
+
+  const bool vec_ok = (N % 32 == 0) && aligned16(qweight);
+  awq::GemvPlan plan;
+  if (!awq::plan_gemv(M, N, K, group_size, d->num_sms, vec_ok, &plan))
+    return fail(AWQ_ERR_UNSUPPORTED, "no decode plan for M=%lld N=%lld K=%lld", (long long)M,
+                (long long)N, (long long)K);
+  const size_t need = awq::gemv_workspace_bytes(plan);
+  if (need > 0 && (!workspace || workspace_bytes < need))
+    return fail(AWQ_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  if (need > 0 && !aligned16(workspace))
+    return fail(AWQ_ERR_INVALID_ARG, "workspace must be 16-byte aligned");
+  cudaError_t e = awq::launch_gemv(plan, x, ldx, qweight, qzeros, scales, out, ldo, (int)M, (int)N,
+                                   (int)K, (int)group_size, workspace, st);
+  if (e != cudaSuccess) return fail_cuda(e, "decode kernel launch");
+  return AWQ_OK;
+}
+
+int awq_gemm_f16(const void* x, int64_t ldx, const int32_t* qweight, const int32_t* qzeros,
+                 const void* scales, void* out, int64_t ldo, int64_t M, int64_t N, int64_t K,
+                 int64_t group_size, void* workspace, size_t workspace_bytes, void* stream) {
+  return awq_gemm_f16_ex(x, ldx, qweight, qzeros, scales, out, ldo, M, N, K, group_size, workspace,
+                         workspace_bytes, stream, AWQ_PATH_AUTO);
+}
+
+int awq_device_status(void* stream, int* status_out) {
+  DeviceInfo* d = nullptr;
+  int rc = device_info(&d);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int v = 0;
+  cudaError_t e = cudaMemcpyAsync(&v, d->status, sizeof(int), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return fail_cuda(e, "reading device status");
+  if (v) {
+    const int zero = 0;
+    e = cudaMemcpyAsync(d->status, &zero, sizeof(int), cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return fail_cuda(e, "clearing device status");
+  }
+  if (status_out) *status_out = v;
+  if (v) return fail(AWQ_ERR_DEVICE, "kernel status word = %d", v);
+  return AWQ_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,46 @@
+// awq_internal.h -- launch interfaces shared between the kernel files and the C-ABI
+// layer (awq_capi.cu).  Not part of the public header.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace awq {
+
+// ---- dequant (awq_dequant.cu) -------------------------------------------------------
+cudaError_t launch_dequant(const int32_t* qweight, const int32_t* qzeros, const void* scales,
+                           void* out, int64_t K, int64_t N, int64_t group_size, int num_sms,
+                           cudaStream_t stream);
+
+// ---- decode / skinny GEMM on mma.sync (awq_gemv.cu) ----------------------------------
+struct GemvPlan {
+  int strips;      // ceil(N / 256): one warp-wide strip of 32 packed words each
+  int splits;      // CTAs along K per strip (split-K)
+  int bps;         // 8-row blocks of K per split
+  int zchunks;     // token chunks of 16 (gridDim.z)
+  int toksets;     // 4-token sets per chunk handled by one CTA (1, 2 or 4)
+  int vec;         // 1: 16-byte loads of 4 packed words (N % 32 == 0, aligned)
+  size_t smem;     // dynamic shared memory per CTA
+  size_t ws_partials_bytes;  // fp32 split-K partials
+  size_t ws_counter_bytes;   // int32 arrival counters (must start at zero)
+};
+
+// Returns false when the shape cannot be planned (the caller reports the error).
+bool plan_gemv(int64_t M, int64_t N, int64_t K, int64_t group_size, int num_sms, bool vec_ok,
+               GemvPlan* plan);
+size_t gemv_workspace_bytes(const GemvPlan& plan);
+cudaError_t launch_gemv(const GemvPlan& plan, const void* x, int64_t ldx, const int32_t* qweight,
+                        const int32_t* qzeros, const void* scales, void* out, int64_t ldo, int M,
+                        int N, int K, int group_size, void* workspace, cudaStream_t stream);
+
+// ---- prefill GEMM on tcgen05 / TMEM (awq_gemm_tc.cu) ----------------------------------
+// Returns true when the tcgen05 kernel can run this shape (alignment / TMA rules).
+bool tc_supported(const void* x, int64_t ldx, const int32_t* qweight, const int32_t* qzeros,
+                  const void* scales, int64_t M, int64_t N, int64_t K, int64_t group_size);
+cudaError_t launch_gemm_tc(const void* x, int64_t ldx, const int32_t* qweight,
+                           const int32_t* qzeros, const void* scales, void* out, int64_t ldo,
+                           int M, int N, int K, int group_size, int num_sms, int* dev_status,
+                           cudaStream_t stream, const char** why);
+
+}  // namespace awq

@@ -1,0 +1,46 @@
+"""Drop-in replacement for songqiuyu/Qwen2-7B-Triton_Engine ``kernels/awq_gemm.py``.
+
+Same module path and names as the reference, so a caller can put this package's
+directory first on ``sys.path`` (``import kernels.awq_gemm``) or assign
+``kernels.awq_gemm.awq_gemm_forward = <this function>`` the way
+``test/compare_benchmark.py:111,120`` swaps implementations.
+
+* ``awq_gemm_forward(x, qweight, qzeros, scales, group_size=128)`` -- reference
+  ``kernels/awq_gemm.py:237-284``.  Same signature, same packed layout, same output
+  shape ``x.shape[:-1] + (N,)`` with ``N = scales.shape[1]``.  M <= 16 runs the
+  sm_100a decode kernel (mma.sync, split-K); larger M runs the tcgen05/TMEM prefill
+  GEMM.  Differences: inputs are validated up front (TypeError / ValueError), a CPU
+  tensor raises instead of running, and no global K*N fp16 buffer is kept.
+* ``_dequant_to_fp16(qweight, qzeros, scales, out_buf, group_size=128)`` --
+  reference ``kernels/awq_gemm.py:66-87``; writes the bit-identical fp16 weights.
+"""
+from __future__ import annotations
+
+import torch
+
+import awq_b200
+
+__all__ = ["awq_gemm_forward", "_dequant_to_fp16"]
+
+
+def _dequant_to_fp16(qweight: torch.Tensor, qzeros: torch.Tensor, scales: torch.Tensor,
+                     out_buf: torch.Tensor, group_size: int = 128) -> torch.Tensor:
+    """AWQ int4 packed weights -> fp16 dense matrix, written into ``out_buf``."""
+    if out_buf.is_contiguous() and out_buf.data_ptr() % 16 == 0:
+        return awq_b200.dequant(qweight, qzeros, scales, group_size, out=out_buf)
+    out_buf.copy_(awq_b200.dequant(qweight, qzeros, scales, group_size))
+    return out_buf
+
+
+def awq_gemm_forward(x: torch.Tensor, qweight: torch.Tensor, qzeros: torch.Tensor,
+                     scales: torch.Tensor, group_size: int = 128) -> torch.Tensor:
+    """AWQ W4A16 product: ``x [..., K] fp16 @ W [K, N]`` -> fp16 ``[..., N]``."""
+    if not isinstance(x, torch.Tensor):
+        raise TypeError("x must be a torch.Tensor")
+    if x.dim() < 1:
+        raise ValueError("x must have at least one dimension")
+    in_shape = x.shape
+    x_flat = x.reshape(-1, x.shape[-1])
+    N = scales.shape[1]
+    out = awq_b200.gemm(x_flat, qweight, qzeros, scales, group_size)
+    return out.view(*in_shape[:-1], N)

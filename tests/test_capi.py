@@ -1,0 +1,87 @@
+"""CPU: the C-ABI library loads, exports what include/awq_b200.h declares, and the
+host-side checks reject bad input before any device work."""
+from __future__ import annotations
+
+import re
+
+import pytest
+import torch
+
+from conftest import REPO
+
+
+def _declared_symbols():
+    text = (REPO / "include" / "awq_b200.h").read_text()
+    return set(re.findall(r"AWQ_API\s+[\w\s\*]+?\b(awq_\w+)\s*\(", text))
+
+
+def test_header_declares_expected_api():
+    syms = _declared_symbols()
+    assert {"awq_dequant_f16", "awq_gemm_f16", "awq_gemm_f16_ex", "awq_gemm_workspace_bytes",
+            "awq_workspace_init", "awq_last_error", "awq_device_status", "awq_version",
+            "awq_tc_supported"} <= syms
+
+
+def test_library_exports_every_declared_symbol():
+    import awq_b200._lib as L
+    lib = L.load()
+    for name in _declared_symbols():
+        assert hasattr(lib, name), name
+    # the binding's signature table covers the whole header
+    assert _declared_symbols() <= set(L.SIGNATURES)
+    assert lib.awq_version() >= 100
+
+
+def test_library_is_the_in_tree_build():
+    import awq_b200
+    assert awq_b200.LIB_PATH.resolve().is_relative_to((REPO / "qwen2-7b-triton_engine_b200").resolve())
+
+
+def test_invalid_arguments_rejected_without_a_device():
+    import awq_b200._lib as L
+    lib = L.load()
+    # null weights: rejected by validation, before any CUDA call
+    rc = lib.awq_gemm_f16(None, 256, None, None, None, None, 64, 1, 64, 256, 128, None, 0, None)
+    assert rc == L.AWQ_ERR_INVALID_ARG
+    assert b"null" in lib.awq_last_error()
+    rc = lib.awq_dequant_f16(16, 16, 16, 16, 256, 60, 128, None)       # N % 8 != 0
+    assert rc == L.AWQ_ERR_INVALID_ARG
+    rc = lib.awq_dequant_f16(16, 16, 16, 16, 200, 64, 128, None)       # K % gs != 0
+    assert rc == L.AWQ_ERR_INVALID_ARG
+    rc = lib.awq_dequant_f16(16, 16, 18, 16, 256, 64, 128, None)       # misaligned scales
+    assert rc == L.AWQ_ERR_INVALID_ARG
+
+
+def _layer(K=256, N=64, gs=128, device="cpu"):
+    qw = torch.zeros((K, N // 8), dtype=torch.int32, device=device)
+    qz = torch.zeros((K // gs, N // 8), dtype=torch.int32, device=device)
+    s = torch.ones((K // gs, N), dtype=torch.float16, device=device)
+    return qw, qz, s
+
+
+def test_dropin_refuses_cpu_tensors():
+    from kernels import awq_gemm
+    qw, qz, s = _layer()
+    with pytest.raises(ValueError, match="CUDA only"):
+        awq_gemm.awq_gemm_forward(torch.zeros(1, 256, dtype=torch.float16), qw, qz, s)
+    with pytest.raises(ValueError, match="CUDA only"):
+        awq_gemm._dequant_to_fp16(qw, qz, s, torch.empty(256, 64, dtype=torch.float16))
+
+
+def test_dropin_signature_matches_reference():
+    import inspect
+    from kernels import awq_gemm
+    sig = inspect.signature(awq_gemm.awq_gemm_forward)
+    assert list(sig.parameters) == ["x", "qweight", "qzeros", "scales", "group_size"]
+    assert sig.parameters["group_size"].default == 128
+    sig = inspect.signature(awq_gemm._dequant_to_fp16)
+    assert list(sig.parameters) == ["qweight", "qzeros", "scales", "out_buf", "group_size"]
+
+
+def test_weight_checks():
+    import awq_b200
+    qw, qz, s = _layer()
+    # shape checks run before the device check only for CUDA tensors; on CPU the
+    # device error comes first and is the one a caller sees
+    with pytest.raises(ValueError):
+        awq_b200.check_weights(qw, qz, s, 128)
