@@ -38,6 +38,11 @@ constexpr int kGemvThreads = kGemvWarps * 32;
 constexpr int kStripN = 256;
 constexpr int kPrefetch = 4;     // blocks of 8 rows in flight per warp
 constexpr int kRedStride = 264;  // padded row of the cross-warp reduction buffer
+// Split-K arrival counters live in a fixed region at the head of the workspace, so a
+// call's fp32 partials (which follow the region) can never land on another call's
+// counters.  One launch uses at most kMaxCounters of them.
+constexpr int kMaxCounters = 16384;
+constexpr size_t kCounterRegionBytes = kMaxCounters * sizeof(int);
 
 __device__ __forceinline__ void mma_16816(float c[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                           uint32_t a3, uint32_t b0, uint32_t b1) {
@@ -302,7 +307,12 @@ bool plan_gemv(int64_t M, int64_t N, int64_t K, int64_t group_size, int num_sms,
     return false;
   GemvPlan p{};
   p.strips = (int)((N + kStripN - 1) / kStripN);
-  p.zchunks = (int)((M + 15) / 16);
+  if (p.strips > kMaxCounters) return false;
+  // token chunks of 16 per launch, bounded so that one launch's counters fit the
+  // fixed counter region; larger M is covered by several launches in stream order
+  const int64_t chunks = (M + 15) / 16;
+  const int64_t max_chunks = kMaxCounters / p.strips;
+  p.zchunks = (int)(chunks < max_chunks ? chunks : max_chunks);
   const int64_t mc = M < 16 ? M : 16;
   p.toksets = mc <= 4 ? 1 : (mc <= 8 ? 2 : 4);
   p.vec = vec_ok ? 1 : 0;
@@ -330,18 +340,19 @@ bool plan_gemv(int64_t M, int64_t N, int64_t K, int64_t group_size, int num_sms,
   if (p.smem > 48 * 1024) return false;
   const size_t NP = (size_t)p.strips * kStripN;
   p.ws_partials_bytes = p.splits > 1 ? (size_t)p.zchunks * p.splits * 16 * NP * sizeof(float) : 0;
-  p.ws_counter_bytes = p.splits > 1 ? align_up((size_t)p.zchunks * p.strips * sizeof(int), 256) : 0;
+  p.ws_counter_bytes = kCounterRegionBytes;
   *plan = p;
   return true;
 }
 
 size_t gemv_workspace_bytes(const GemvPlan& plan) {
-  return plan.ws_counter_bytes + align_up(plan.ws_partials_bytes, 256);
+  if (plan.splits <= 1) return 0;
+  return kCounterRegionBytes + align_up(plan.ws_partials_bytes, 256);
 }
 
 template <int TOKSETS>
-static void launch_t(const GemvPlan& plan, const GemvArgs& args, cudaStream_t stream) {
-  dim3 grid(plan.strips, plan.splits, plan.zchunks);
+static void launch_t(const GemvPlan& plan, const GemvArgs& args, int zchunks, cudaStream_t stream) {
+  dim3 grid(plan.strips, plan.splits, zchunks);
   if (plan.vec)
     gemv_kernel<TOKSETS, true><<<grid, kGemvThreads, plan.smem, stream>>>(args);
   else
@@ -352,23 +363,32 @@ cudaError_t launch_gemv(const GemvPlan& plan, const void* x, int64_t ldx, const 
                         const int32_t* qzeros, const void* scales, void* out, int64_t ldo, int M,
                         int N, int K, int group_size, void* workspace, cudaStream_t stream) {
   GemvArgs a;
-  a.x = static_cast<const __half*>(x);
   a.ldx = ldx;
   a.qw = qweight;
   a.qz = qzeros;
   a.scales = static_cast<const __half*>(scales);
-  a.out = static_cast<__half*>(out);
   a.ldo = ldo;
-  a.M = M; a.N = N; a.K = K; a.gs = group_size; a.PN = N / 8;
+  a.N = N; a.K = K; a.gs = group_size; a.PN = N / 8;
   a.strips = plan.strips; a.splits = plan.splits; a.bps = plan.bps;
   a.counters = reinterpret_cast<int*>(workspace);
-  a.ws = reinterpret_cast<float*>(static_cast<char*>(workspace) + plan.ws_counter_bytes);
-  switch (plan.toksets) {
-    case 1: launch_t<1>(plan, a, stream); break;
-    case 2: launch_t<2>(plan, a, stream); break;
-    default: launch_t<4>(plan, a, stream); break;
+  a.ws = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterRegionBytes);
+  // one launch per group of plan.zchunks token chunks (16 tokens each)
+  const int64_t rows_per_launch = (int64_t)plan.zchunks * 16;
+  for (int64_t m0 = 0; m0 < M; m0 += rows_per_launch) {
+    const int64_t mrows = (M - m0 < rows_per_launch) ? (M - m0) : rows_per_launch;
+    a.x = static_cast<const __half*>(x) + m0 * ldx;
+    a.out = static_cast<__half*>(out) + m0 * ldo;
+    a.M = (int)mrows;
+    const int z = (int)((mrows + 15) / 16);
+    switch (plan.toksets) {
+      case 1: launch_t<1>(plan, a, z, stream); break;
+      case 2: launch_t<2>(plan, a, z, stream); break;
+      default: launch_t<4>(plan, a, z, stream); break;
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
   }
-  return cudaGetLastError();
+  return cudaSuccess;
 }
 
 }  // namespace awq
