@@ -1,18 +1,333 @@
-// awq_gemm_tc.cu -- placeholder until the tcgen05 prefill kernel lands.
+// awq_gemm_tc.cu -- prefill AWQ W4A16 GEMM on the sm_100a tensor cores (tcgen05 + TMEM).
+//
+// Replaces _awq_gemm_kernel (songqiuyu/Qwen2-7B-Triton_Engine kernels/awq_gemm.py:152-228,
+// 64x64 tiles on mma.sync) for M > 16.  One CTA computes a 128 x 256 tile of
+// out = x @ W with fp32 accumulation in tensor memory:
+//
+//   warp 0      TMA producer: per 64-deep K step loads the x tile (128 x 64 fp16,
+//               128-byte swizzle), the packed weight tile (64 rows x 32 words), one
+//               row of scales (256 fp16) and one row of packed zeros (32 words)
+//               into a 3-stage shared-memory ring, completion on full[s]
+//   warps 2..5  dequant: int4 -> fp16 W tile, bit-exact (fp16 (w - z) * scale),
+//               written as the UMMA B operand in the MN-major 128-byte-swizzled
+//               canonical layout, then fence.proxy.async + arrive on deq[s];
+//               after the K loop the same warps run the epilogue
+//   warp 1      TMEM allocation (256 columns) and the single-thread MMA issue:
+//               4 x tcgen05.mma.kind::f16 (M=128, N=256, K=16) per stage, then
+//               tcgen05.commit -> empty[s] frees the stage; the last commit
+//               signals the accumulator to the epilogue
+//   epilogue    tcgen05.ld 32x32b (each warp its 32 TMEM lanes = 32 rows),
+//               fp32 -> fp16, 16-byte global stores (rows >= M / cols >= N masked)
+//
+// Shapes it takes (tc_supported): N % 32 == 0, group_size % 64 == 0 (so a K step
+// lies in one group), ldx % 8 == 0 and 16-byte aligned pointers (TMA rules).
+// Every mbarrier wait is bounded; a time-out sets the status word and the CTA
+// drains its in-flight copies and MMAs, frees TMEM and exits.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "awq_common.cuh"
 #include "awq_internal.h"
+#include "awq_sm100.cuh"
 
 namespace awq {
 
-bool tc_supported(const void*, int64_t, const int32_t*, const int32_t*, const void*, int64_t,
-                  int64_t, int64_t, int64_t) {
-  return false;
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 3;
+constexpr int kThreads = 192;
+constexpr uint32_t A_BYTES = BM * BK * 2;        // 16 KB
+constexpr uint32_t B_BYTES = BN * BK * 2;        // 32 KB
+constexpr uint32_t RAW_BYTES = BK * (BN / 8) * 4; // 8 KB
+constexpr uint32_t SC_BYTES = BN * 2;             // 512 B
+constexpr uint32_t ZR_BYTES = (BN / 8) * 4;       // 128 B
+constexpr uint32_t TX_BYTES = A_BYTES + RAW_BYTES + SC_BYTES + ZR_BYTES;
+// B operand (MN-major, 128-byte swizzle): atom = 64 n x 8 k (1 KB); k-groups of 8
+// are SBO = 1 KB apart, 64-wide n atoms LBO = 8 KB apart.
+constexpr uint32_t B_SBO = 1024, B_LBO = 8 * 1024;
+constexpr uint32_t A_SBO = 1024;                  // K-major: 8-row groups 1 KB apart
+constexpr uint32_t kIdesc = sm100::idesc_f16_f32(BM, BN, /*a_mn*/ 0, /*b_mn*/ 1);
+constexpr uint32_t TMEM_COLS = 256;
+
+constexpr uint32_t OFF_A = 0;
+constexpr uint32_t OFF_B = OFF_A + STAGES * A_BYTES;
+constexpr uint32_t OFF_RAW = OFF_B + STAGES * B_BYTES;
+constexpr uint32_t OFF_SC = OFF_RAW + STAGES * RAW_BYTES;
+constexpr uint32_t OFF_ZR = OFF_SC + STAGES * SC_BYTES;
+constexpr uint32_t OFF_BAR = OFF_ZR + STAGES * ZR_BYTES;    // full, deq, empty, accf
+constexpr uint32_t OFF_MISC = OFF_BAR + (3 * STAGES + 1) * 8;
+constexpr uint32_t SMEM_BYTES = OFF_MISC + 16 + 1024;       // + alignment slack
+
+struct TcArgs {
+  __half* out;
+  int64_t ldo;
+  int M, N, K, gs;
+  int* status;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+               const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmZ,
+               const TcArgs args) {
+  extern __shared__ unsigned char smem_raw[];
+  const uint32_t base_raw = sm100::smem_u32(smem_raw);
+  const uint32_t sbase = (base_raw + 1023u) & ~1023u;        // 1 KB aligned (swizzle atoms)
+  unsigned char* sgen = smem_raw + (sbase - base_raw);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int tile_m = blockIdx.x, tile_n = blockIdx.y;
+  const int KT = args.K / BK;
+
+  auto bar_full = [&](int s) { return sbase + OFF_BAR + 8u * s; };
+  auto bar_deq = [&](int s) { return sbase + OFF_BAR + 8u * (STAGES + s); };
+  auto bar_empty = [&](int s) { return sbase + OFF_BAR + 8u * (2 * STAGES + s); };
+  const uint32_t bar_accf = sbase + OFF_BAR + 8u * (3 * STAGES);
+  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(sgen + OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sgen + OFF_MISC + 4);
+
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      sm100::mbar_init(bar_full(s), 1);
+      sm100::mbar_init(bar_deq(s), 4);        // one arrive per dequant warp
+      sm100::mbar_init(bar_empty(s), 1);
+    }
+    sm100::mbar_init(bar_accf, 1);
+    sm100::fence_mbar_init();
+    *abort_flag = 0;
+    sm100::prefetch_tmap(&tmA);
+    sm100::prefetch_tmap(&tmW);
+    sm100::prefetch_tmap(&tmS);
+    sm100::prefetch_tmap(&tmZ);
+  }
+  if (warp == 1) {
+    sm100::tmem_alloc(sbase + OFF_MISC, TMEM_COLS);
+    sm100::tmem_relinquish();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem_d = *tmem_slot;
+
+  int issued_mma = 0;
+  if (warp == 0) {
+    // ------------------------------------------------------------- TMA producer ----
+    if (lane == 0) {
+      int kt = 0;
+      for (; kt < KT; ++kt) {
+        const int s = kt % STAGES;
+        if (kt >= STAGES &&
+            !sm100::mbar_wait_bounded(bar_empty(s), ((kt / STAGES) & 1) ^ 1, args.status)) {
+          *abort_flag = 1;
+          break;
+        }
+        if (*abort_flag) break;
+        const int k0 = kt * BK;
+        const int grp = k0 / args.gs;
+        sm100::mbar_arrive_expect_tx(bar_full(s), TX_BYTES);
+        sm100::tma_load_2d(sbase + OFF_A + s * A_BYTES, &tmA, bar_full(s), k0, tile_m * BM);
+        sm100::tma_load_2d(sbase + OFF_RAW + s * RAW_BYTES, &tmW, bar_full(s), tile_n * (BN / 8), k0);
+        sm100::tma_load_2d(sbase + OFF_SC + s * SC_BYTES, &tmS, bar_full(s), tile_n * BN, grp);
+        sm100::tma_load_2d(sbase + OFF_ZR + s * ZR_BYTES, &tmZ, bar_full(s), tile_n * (BN / 8), grp);
+      }
+      // drain: the copies of the last (up to) STAGES steps must land before exit
+      for (int j = (kt > STAGES ? kt - STAGES : 0); j < kt; ++j)
+        sm100::mbar_wait_bounded(bar_full(j % STAGES), (j / STAGES) & 1, args.status);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------- MMA issuer ------
+    if (lane == 0) {
+      for (int kt = 0; kt < KT; ++kt) {
+        const int s = kt % STAGES;
+        if (!sm100::mbar_wait_bounded(bar_deq(s), (kt / STAGES) & 1, args.status)) {
+          *abort_flag = 1;
+          break;
+        }
+        if (*abort_flag) break;
+        sm100::tc_fence_after();
+        const uint32_t a0 = sbase + OFF_A + s * A_BYTES;
+        const uint32_t b0 = sbase + OFF_B + s * B_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          const uint64_t ad = sm100::umma_desc_sw128(a0 + kk * 32, 16, A_SBO);
+          const uint64_t bd = sm100::umma_desc_sw128(b0 + kk * 2 * B_SBO, B_LBO, B_SBO);
+          sm100::umma_f16(tmem_d, ad, bd, kIdesc, (kt | kk) != 0);
+        }
+        sm100::umma_commit(bar_empty(s));
+        issued_mma = 1;
+      }
+      sm100::umma_commit(bar_accf);     // arrives when every issued MMA has completed
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------- dequant ---------
+    const int dw = warp - 2;                 // 0..3: rows [16 dw, 16 dw + 16) of a K step
+    const int w = lane;                      // packed word column within the tile
+    const uint32_t bst_atom = (uint32_t)(w >> 3) * B_LBO;
+    for (int kt = 0; kt < KT; ++kt) {
+      const int s = kt % STAGES;
+      if (!sm100::mbar_wait_bounded(bar_full(s), (kt / STAGES) & 1, args.status)) {
+        *abort_flag = 1;
+        break;
+      }
+      if (*abort_flag) break;
+      const uint32_t* raw = reinterpret_cast<const uint32_t*>(sgen + OFF_RAW + s * RAW_BYTES);
+      const uint32_t zw = reinterpret_cast<const uint32_t*>(sgen + OFF_ZR + s * ZR_BYTES)[w];
+      const uint4 s4 = reinterpret_cast<const uint4*>(sgen + OFF_SC + s * SC_BYTES)[w];
+      uint32_t zc[4], sc[4] = {s4.x, s4.y, s4.z, s4.w};
+      zero_consts(zw, zc);
+      const uint32_t bstage = sbase + OFF_B + s * B_BYTES + bst_atom;
+#pragma unroll 4
+      for (int i = 0; i < 16; ++i) {
+        const int r = dw * 16 + i;           // K row within the step
+        uint32_t d[4];
+        dequant_word(raw[r * (BN / 8) + w], zc, sc, d);
+        const uint32_t addr = bstage + (uint32_t)(r >> 3) * B_SBO + (uint32_t)(r & 7) * 128u +
+                              ((uint32_t)((w & 7) ^ (r & 7)) << 4);
+        sm100::st_shared_v4(addr, d[0], d[1], d[2], d[3]);
+      }
+      sm100::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(bar_deq(s));
+    }
+
+    // ------------------------------------------------------------- epilogue --------
+    const bool ok = sm100::mbar_wait_bounded(bar_accf, 0, args.status);
+    sm100::tc_fence_after();
+    if (ok && !*abort_flag) {
+      const int q = warp & 3;                  // TMEM lane quarter this warp may access
+      const int row = tile_m * BM + q * 32 + lane;
+      const uint32_t taddr = tmem_d + ((uint32_t)(q * 32) << 16);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t v[32];
+        sm100::tmem_ld_32x32b_x32(taddr + c * 32, v);
+        sm100::tmem_ld_wait();
+        const int col = tile_n * BN + c * 32;
+        if (row < args.M && col < args.N) {
+          uint32_t h[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            h[j] = h2_as_u32(__floats2half2_rn(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1])));
+          uint4* dst = reinterpret_cast<uint4*>(args.out + (int64_t)row * args.ldo + col);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            dst[j] = make_uint4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
+        }
+      }
+    }
+  }
+  (void)issued_mma;
+
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    // in the abort path the accumulator commit may still be in flight: wait for it
+    // (bounded) before giving the columns back
+    if (*abort_flag) sm100::mbar_wait_bounded(bar_accf, 0, nullptr, 100000000ull);
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem_d, TMEM_COLS);
+  }
 }
 
-cudaError_t launch_gemm_tc(const void*, int64_t, const int32_t*, const int32_t*, const void*,
-                           void*, int64_t, int, int, int, int, int, int*, cudaStream_t,
-                           const char** why) {
-  *why = "not built";
-  return cudaSuccess;
+// ---------------------------------------------------------------------------------
+// host: tensor maps through the driver entry point (no link-time libcuda dependency)
+// ---------------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+bool make_map_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* ptr, uint64_t inner,
+                 uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+                 CUtensorMapSwizzle swz) {
+  EncodeTiledFn enc = get_encode();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+
+bool tc_supported(const void* x, int64_t ldx, const int32_t* qweight, const int32_t* qzeros,
+                  const void* scales, int64_t M, int64_t N, int64_t K, int64_t group_size) {
+  if (M < 1 || N < 32 || K < BK) return false;
+  if (N % 32 || group_size % BK || K % group_size) return false;
+  if (ldx % 8 || ldx < K) return false;
+  if (!al16(x) || !al16(qweight) || !al16(qzeros) || !al16(scales)) return false;
+  if (M > (1 << 30) || N > (1 << 30) || K > (1 << 30)) return false;
+  return get_encode() != nullptr;
+}
+
+cudaError_t launch_gemm_tc(const void* x, int64_t ldx, const int32_t* qweight,
+                           const int32_t* qzeros, const void* scales, void* out, int64_t ldo,
+                           int M, int N, int K, int group_size, int num_sms, int* dev_status,
+                           cudaStream_t stream, const char** why) {
+  (void)num_sms;
+  *why = nullptr;
+  if (!tc_supported(x, ldx, qweight, qzeros, scales, M, N, K, group_size)) {
+    *why = "shape or alignment not supported";
+    return cudaSuccess;
+  }
+  if (ldo % 8 || !al16(out)) {
+    *why = "out must be 16-byte aligned with ldo % 8 == 0";
+    return cudaSuccess;
+  }
+  CUtensorMap tmA, tmW, tmS, tmZ;
+  const int G = K / group_size;
+  bool ok = make_map_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, K, M, (uint64_t)ldx * 2, BK, BM,
+                        CU_TENSOR_MAP_SWIZZLE_128B) &&
+            make_map_2d(&tmW, CU_TENSOR_MAP_DATA_TYPE_INT32, qweight, N / 8, K, (uint64_t)N / 2,
+                        BN / 8, BK, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+            make_map_2d(&tmS, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, scales, N, G, (uint64_t)N * 2, BN, 1,
+                        CU_TENSOR_MAP_SWIZZLE_NONE) &&
+            make_map_2d(&tmZ, CU_TENSOR_MAP_DATA_TYPE_INT32, qzeros, N / 8, G, (uint64_t)N / 2,
+                        BN / 8, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (!ok) {
+    *why = "cuTensorMapEncodeTiled failed";
+    return cudaSuccess;
+  }
+  static std::once_flag attr_once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(attr_once, [] {
+    attr_err = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)SMEM_BYTES);
+  });
+  if (attr_err != cudaSuccess) return attr_err;
+  TcArgs a;
+  a.out = static_cast<__half*>(out);
+  a.ldo = ldo;
+  a.M = M; a.N = N; a.K = K; a.gs = group_size;
+  a.status = dev_status;
+  dim3 grid((M + BM - 1) / BM, (N + BN - 1) / BN);
+  gemm_tc_kernel<<<grid, kThreads, SMEM_BYTES, stream>>>(tmA, tmW, tmS, tmZ, a);
+  return cudaGetLastError();
 }
 
 }  // namespace awq
