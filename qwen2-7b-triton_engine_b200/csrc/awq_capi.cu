@@ -10,6 +10,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -41,6 +42,7 @@ __device__ int g_device_status;   // one per device; kernels OR their error bits
 constexpr int kMaxDevices = 64;
 struct DeviceInfo {
   int num_sms = 0;
+  int max_cluster = 8;     // largest thread-block cluster the decode kernel may use
   int* status = nullptr;
   bool ready = false;
 };
@@ -68,6 +70,10 @@ int device_info(DeviceInfo** out) {
     if (e != cudaSuccess) return fail_cuda(e, "cudaGetSymbolAddress(status)");
     d.num_sms = sms;
     d.status = static_cast<int*>(p);
+    if (const char* env = getenv("AWQ_MAX_CLUSTER")) {
+      int v = atoi(env);
+      if (v == 1 || v == 2 || v == 4 || v == 8 || v == 16) d.max_cluster = v;
+    }
     d.ready = true;
   }
   *out = &d;
@@ -169,6 +175,15 @@ int awq_gemm_f16_ex(const void* x, int64_t ldx, const int32_t* qweight, const in
                                         (int)K, (int)group_size, d->num_sms, d->status, st, &why);
     if (why) return fail(AWQ_ERR_UNSUPPORTED, "tcgen05 path: %s", why);
     if (e != cudaSuccess) return fail_cuda(e, "tcgen05 GEMM launch");
+    return AWQ_OK;
+  }
+
+  const int max_cs = d->max_cluster;
+  if (awq::gemv_tma_supported(qweight, N, ldx, x) &&
+      awq::gemv_tma_smem_bytes(M, N, K, d->num_sms, max_cs) <= awq::kGemvTmaMaxSmem) {
+    cudaError_t e = awq::launch_gemv_tma(x, ldx, qweight, qzeros, scales, out, ldo, (int)M, (int)N,
+                                         (int)K, (int)group_size, d->num_sms, max_cs, d->status, st);
+    if (e != cudaSuccess) return fail_cuda(e, "decode (TMA) kernel launch");
     return AWQ_OK;
   }
 
