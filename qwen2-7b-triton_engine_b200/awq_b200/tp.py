@@ -1,0 +1,179 @@
+"""Single-box tensor parallelism for the AWQ linears (one process per GPU, NCCL).
+
+The reference runs on one GPU and has no parallelism (inference/engine.py:15,
+model/config.py:24).  This module adds the standard Megatron split on top of the
+AWQ drop-in, in the packed layout the reference registers (model/qwen2.py:34-36):
+
+* column parallel (q/k/v, gate, up): rank r keeps output columns [n0, n1) -- whole
+  packed words, so qweight[:, n0/8:n1/8], qzeros[:, n0/8:n1/8], scales[:, n0:n1].
+  No communication.  For the fused gate+up matrix (model/qwen2.py:176-178) gate and
+  up are sliced with the same bounds, so SiLU(gate) * up stays local to the rank.
+* row parallel (o, down): rank r keeps K rows [k0, k1) in whole quantization groups
+  (qweight[k0:k1], qzeros/scales[k0/gs:k1/gs]); groups are dealt out as evenly as
+  possible (Qwen2-7B down has 148 groups: 19/18 at 8 ranks).  Each rank's product is
+  a partial sum and one all-reduce (sum) of the fp16 [M, N] output finishes it.
+
+The product runs through ``kernels.awq_gemm.awq_gemm_forward`` (the sm_100a
+library); ``gemm=`` lets host-logic tests substitute a CPU function under ``gloo``.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable, Optional
+
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+
+GemmFn = Callable[[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, int], torch.Tensor]
+
+
+def _default_gemm() -> GemmFn:
+    from kernels.awq_gemm import awq_gemm_forward
+    return awq_gemm_forward
+
+
+def even_split(total: int, parts: int, rank: int) -> tuple[int, int]:
+    """[lo, hi) of `rank` when `total` units are dealt as evenly as possible."""
+    base, extra = divmod(total, parts)
+    lo = rank * base + min(rank, extra)
+    return lo, lo + base + (1 if rank < extra else 0)
+
+
+def column_bounds(N: int, world: int, rank: int) -> tuple[int, int]:
+    """Column shard [n0, n1) in whole packed words (multiples of 8 columns)."""
+    if N % 8:
+        raise ValueError(f"N={N} is not a multiple of 8")
+    w0, w1 = even_split(N // 8, world, rank)
+    return w0 * 8, w1 * 8
+
+
+def row_bounds(K: int, group_size: int, world: int, rank: int) -> tuple[int, int]:
+    """Row shard [k0, k1) in whole quantization groups."""
+    if K % group_size:
+        raise ValueError(f"K={K} is not a multiple of group_size={group_size}")
+    g0, g1 = even_split(K // group_size, world, rank)
+    return g0 * group_size, g1 * group_size
+
+
+def shard_columns(qweight, qzeros, scales, n0: int, n1: int):
+    return (qweight[:, n0 // 8:n1 // 8].contiguous(), qzeros[:, n0 // 8:n1 // 8].contiguous(),
+            scales[:, n0:n1].contiguous())
+
+
+def shard_rows(qweight, qzeros, scales, k0: int, k1: int, group_size: int):
+    return (qweight[k0:k1].contiguous(), qzeros[k0 // group_size:k1 // group_size].contiguous(),
+            scales[k0 // group_size:k1 // group_size].contiguous())
+
+
+def shard_fused_columns(qweight, qzeros, scales, parts: list[int], world: int, rank: int,
+                        bounds: Optional[Callable[[int, int, int], tuple[int, int]]] = None):
+    """Column shard of a matrix that concatenates several projections along N
+    (fused gate+up, fused q/k/v): each part is split on its own and the rank's
+    slices are concatenated again, so part boundaries survive sharding.
+    `bounds(width, world, rank)` gives a part's [lo, hi); default: whole words."""
+    bounds = bounds or column_bounds
+    out_qw, out_qz, out_s, off = [], [], [], 0
+    for width in parts:
+        a, b = bounds(width, world, rank)
+        qw, qz, s = shard_columns(qweight, qzeros, scales, off + a, off + b)
+        out_qw.append(qw), out_qz.append(qz), out_s.append(s)
+        off += width
+    if off != scales.shape[1]:
+        raise ValueError(f"parts {parts} do not add up to N={scales.shape[1]}")
+    return torch.cat(out_qw, 1), torch.cat(out_qz, 1), torch.cat(out_s, 1)
+
+
+@dataclass
+class AWQWeights:
+    qweight: torch.Tensor
+    qzeros: torch.Tensor
+    scales: torch.Tensor
+    group_size: int = 128
+    bias: Optional[torch.Tensor] = None
+
+
+class ColumnParallelAWQ:
+    """Rank's column slice of an AWQ linear (optionally a fused multi-part one)."""
+
+    def __init__(self, full: AWQWeights, world: int, rank: int, parts: Optional[list[int]] = None,
+                 gemm: Optional[GemmFn] = None, bounds=None):
+        parts = parts or [full.scales.shape[1]]
+        bounds = bounds or column_bounds
+        self.parts_local = [bounds(p, world, rank)[1] - bounds(p, world, rank)[0] for p in parts]
+        qw, qz, s = shard_fused_columns(full.qweight, full.qzeros, full.scales, parts, world, rank,
+                                        bounds)
+        bias = None
+        if full.bias is not None:
+            pieces, off = [], 0
+            for p in parts:
+                a, b = bounds(p, world, rank)
+                pieces.append(full.bias[off + a:off + b])
+                off += p
+            bias = torch.cat(pieces)
+        self.w = AWQWeights(qw, qz, s, full.group_size, bias)
+        self.gemm = gemm or _default_gemm()
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        out = self.gemm(x, self.w.qweight, self.w.qzeros, self.w.scales, self.w.group_size)
+        if self.w.bias is not None:                   # bias added after the GEMM (model/qwen2.py:45-46)
+            out = out + self.w.bias
+        return out
+
+
+class RowParallelAWQ:
+    """Rank's K-row slice of an AWQ linear; the partial outputs are all-reduced."""
+
+    def __init__(self, full: AWQWeights, world: int, rank: int, group: Optional[object] = None,
+                 gemm: Optional[GemmFn] = None):
+        K = full.qweight.shape[0]
+        self.k0, self.k1 = row_bounds(K, full.group_size, world, rank)
+        qw, qz, s = shard_rows(full.qweight, full.qzeros, full.scales, self.k0, self.k1,
+                               full.group_size)
+        self.w = AWQWeights(qw, qz, s, full.group_size, full.bias if rank == 0 else None)
+        self.group = group
+        self.world = world
+        self.gemm = gemm or _default_gemm()
+
+    def __call__(self, x_local: torch.Tensor) -> torch.Tensor:
+        """x_local holds this rank's K columns [k0, k1) of the activation."""
+        if self.k1 > self.k0:
+            out = self.gemm(x_local, self.w.qweight, self.w.qzeros, self.w.scales,
+                            self.w.group_size)
+        else:                                         # more ranks than groups
+            out = torch.zeros((*x_local.shape[:-1], self.w.scales.shape[1]),
+                              dtype=torch.float16, device=x_local.device)
+        if self.w.bias is not None:
+            out = out + self.w.bias
+        if self.world > 1:
+            dist.all_reduce(out, op=dist.ReduceOp.SUM, group=self.group)
+        return out
+
+
+class TensorParallelMLP:
+    """Qwen2 MLP (model/qwen2.py:160-197) over `world` ranks: fused gate+up column
+    parallel, SiLU(gate) * up local, down row parallel + all-reduce.
+
+    The intermediate dimension is split in whole quantization groups, so a rank's
+    gate/up columns [lo, hi) are exactly the K rows of down it holds."""
+
+    def __init__(self, gate_up: AWQWeights, down: AWQWeights, intermediate: int, world: int,
+                 rank: int, group: Optional[object] = None, gemm: Optional[GemmFn] = None):
+        if down.qweight.shape[0] != intermediate:
+            raise ValueError("down must have K == intermediate")
+        gs = down.group_size
+
+        def bounds(width, w, r):
+            return row_bounds(width, gs, w, r)
+
+        self.gate_up = ColumnParallelAWQ(gate_up, world, rank, parts=[intermediate, intermediate],
+                                         gemm=gemm, bounds=bounds)
+        self.inter_local = self.gate_up.parts_local[0]
+        self.down = RowParallelAWQ(down, world, rank, group=group, gemm=gemm)
+        assert (self.down.k1 - self.down.k0) == self.inter_local
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        gu = self.gate_up(x)
+        gate, up = gu[..., :self.inter_local], gu[..., self.inter_local:]
+        h = (F.silu(gate.float()) * up.float()).to(torch.float16)
+        return self.down(h)

@@ -175,6 +175,21 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
 
   uint32_t zcst[4][4], scl[4][4];
   int grp_end = -1;
+  // raw zeros / scales of the next group, loaded one group ahead
+  uint4 pf_z = make_uint4(0, 0, 0, 0), pf_s[4];
+  int pf_grp = -1;
+  auto load_group = [&](int grp) {
+    pf_grp = grp;
+    pf_z = make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) pf_s[c] = make_uint4(0, 0, 0, 0);
+    if (wc0 < a.PN) {
+      pf_z = __ldg(reinterpret_cast<const uint4*>(a.qz + (int64_t)grp * a.PN + wc0));
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        pf_s[c] = __ldg(reinterpret_cast<const uint4*>(a.scales + (int64_t)grp * a.N + (wc0 + c) * 8));
+    }
+  };
   auto flush = [&]() {
     if constexpr (SPOST) {
 #pragma unroll
@@ -207,18 +222,16 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
     if (k0 >= grp_end) {
       if (grp_end >= 0) flush();
       const int grp = k0 / a.gs;
+      if (grp != pf_grp) load_group(grp);           // first group of the warp's range
       grp_end = (grp + 1) * a.gs;
-      const uint4 z4 = (wc0 < a.PN) ? __ldg(reinterpret_cast<const uint4*>(a.qz + (int64_t)grp * a.PN + wc0))
-                                    : make_uint4(0, 0, 0, 0);
-      const uint32_t zw[4] = {z4.x, z4.y, z4.z, z4.w};
+      const uint32_t zw[4] = {pf_z.x, pf_z.y, pf_z.z, pf_z.w};
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        uint4 s4 = make_uint4(0, 0, 0, 0);
-        if (wc0 < a.PN)
-          s4 = __ldg(reinterpret_cast<const uint4*>(a.scales + (int64_t)grp * a.N + (wc0 + c) * 8));
         zero_consts(zw[c], zcst[c]);
-        scl[c][0] = s4.x; scl[c][1] = s4.y; scl[c][2] = s4.z; scl[c][3] = s4.w;
+        scl[c][0] = pf_s[c].x; scl[c][1] = pf_s[c].y; scl[c][2] = pf_s[c].z; scl[c][3] = pf_s[c].w;
       }
+      // fetch the next group now; it has a whole group of blocks to arrive
+      if (grp_end < b1 * 8) load_group(grp + 1);
     }
     uint32_t bf0[TOKSETS], bf1[TOKSETS];
     const int kl = k0 - krow0;
@@ -255,10 +268,10 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
         }
       }
     }
-    // refill this stage with block i + kStages (all lanes have consumed it)
+    // refill this stage with block i + kStages: every lane's reads of it have
+    // completed (their values were consumed above), so the copy may overwrite it
     __syncwarp();
     if (lane == 0 && i + kStages < nblk) {
-      sm100::fence_proxy_async_smem();
       sm100::mbar_arrive_expect_tx(bars + 8 * s, kStageBytes);
       sm100::tma_load_2d(st, &tmW, bars + 8 * s, strip * 32, (b0 + i + kStages) * 8);
     }

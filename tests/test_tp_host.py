@@ -1,0 +1,159 @@
+"""CPU: host logic of the tensor-parallel wrapper (awq_b200.tp) with world_size-2 `gloo`
+process groups.  The GEMM is the CPU oracle here (injected through ``gemm=``); on GPUs
+the same classes call the sm_100a library and NCCL."""
+from __future__ import annotations
+
+import os
+import socket
+import time
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import oracle as O
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _cpu_gemm(x, qw, qz, s, gs):
+    return O.torch_awq_gemm_f32(x, qw, qz, s, gs).to(torch.float16)
+
+
+def _layer(K, N, seed, gs=128):
+    qw, qz, s = O.make_awq_layer(K, N, gs, seed=seed)
+    return torch.from_numpy(qw), torch.from_numpy(qz), torch.from_numpy(s)
+
+
+def test_bounds_partition_exactly():
+    from awq_b200 import tp
+    for world in (1, 2, 3, 4, 8):
+        for N in (512, 4608, 37888, 3584):
+            b = [tp.column_bounds(N, world, r) for r in range(world)]
+            assert b[0][0] == 0 and b[-1][1] == N
+            assert all(b[i][1] == b[i + 1][0] for i in range(world - 1))
+            assert all(lo % 8 == 0 for lo, _ in b)
+        for K in (3584, 18944):
+            b = [tp.row_bounds(K, 128, world, r) for r in range(world)]
+            assert b[0][0] == 0 and b[-1][1] == K
+            assert all(lo % 128 == 0 and hi % 128 == 0 for lo, hi in b)
+            sizes = [hi - lo for lo, hi in b]
+            assert max(sizes) - min(sizes) <= 128
+    # Qwen2-7B down at 8 ranks: 148 groups -> 19/18
+    assert [tp.row_bounds(18944, 128, 8, r)[1] - tp.row_bounds(18944, 128, 8, r)[0]
+            for r in range(8)] == [2432] * 4 + [2304] * 4
+
+
+def test_fused_column_shards_keep_parts_aligned():
+    from awq_b200 import tp
+    inter = 512
+    qw, qz, s = _layer(256, 2 * inter, seed=3)
+    full = O.awq_dequant(qw.numpy(), qz.numpy(), s.numpy())
+    for world in (2, 4):
+        for r in range(world):
+            lo, hi = tp.row_bounds(inter, 128, world, r)
+            sqw, sqz, ss = tp.shard_fused_columns(
+                qw, qz, s, [inter, inter], world, r, bounds=lambda w, ww, rr: tp.row_bounds(w, 128, ww, rr))
+            got = O.awq_dequant(sqw.numpy(), sqz.numpy(), ss.numpy())
+            import numpy as np
+            want = np.concatenate([full[:, lo:hi], full[:, inter + lo:inter + hi]], axis=1)
+            assert np.array_equal(got.view(np.uint16), want.view(np.uint16))
+
+
+def _worker(rank, world, port, K, inter, hidden, seed, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=30))
+    try:
+        from awq_b200 import tp
+        gu = _layer(hidden, 2 * inter, seed)
+        dn = _layer(inter, hidden, seed + 1)
+        o = _layer(hidden, hidden, seed + 2)
+        x = torch.from_numpy(O.make_x(3, hidden, seed=seed + 3))
+        mlp = tp.TensorParallelMLP(tp.AWQWeights(*gu), tp.AWQWeights(*dn), inter, world, rank,
+                                   gemm=_cpu_gemm)
+        y = mlp(x)
+        ro = tp.RowParallelAWQ(tp.AWQWeights(*o), world, rank, gemm=_cpu_gemm)
+        z = ro(x[:, ro.k0:ro.k1].contiguous())
+        q.put((rank, y.float().numpy(), z.float().numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp_mlp_and_row_parallel_gloo_world2():
+    world, K, inter, hidden, seed = 2, 256, 512, 256, 11
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, K, inter, hidden, seed, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    for _ in range(world):
+        rank, y, z = q.get(timeout=120)
+        results[rank] = (y, z)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    # unsharded reference
+    gu = _layer(hidden, 2 * inter, seed)
+    dn = _layer(inter, hidden, seed + 1)
+    o = _layer(hidden, hidden, seed + 2)
+    x = torch.from_numpy(O.make_x(3, hidden, seed=seed + 3))
+    g = _cpu_gemm(x, *gu, 128)
+    h = (torch.nn.functional.silu(g[:, :inter].float()) * g[:, inter:].float()).half()
+    y_ref = _cpu_gemm(h, *dn, 128).float().numpy()
+    z_ref = _cpu_gemm(x, *o, 128).float().numpy()
+    for rank in range(world):
+        y, z = results[rank]
+        assert O.max_rel_err(y, y_ref) <= 1e-2
+        assert O.max_rel_err(z, z_ref) <= 1e-2
+
+
+def _failing_worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=4))
+    if rank == 1:
+        q.put((rank, "raised"))
+        q.close()
+        q.join_thread()                    # flush the message before dying
+        os._exit(3)                        # a rank that dies between steps
+    try:
+        from awq_b200 import tp
+        o = _layer(256, 128, 5)
+        ro = tp.RowParallelAWQ(tp.AWQWeights(*o), world, rank, gemm=_cpu_gemm)
+        x = torch.from_numpy(O.make_x(1, 256, seed=1))
+        ro(x[:, ro.k0:ro.k1].contiguous())
+        q.put((rank, "no error"))
+    except Exception as e:                 # the collective must fail, not hang
+        q.put((rank, f"error: {type(e).__name__}"))
+    q.close()
+    q.join_thread()
+    os._exit(0)
+
+
+def test_dead_rank_surfaces_as_error_not_hang():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, 2, port, q)) for r in range(2)]
+    t0 = time.time()
+    for p in procs:
+        p.start()
+    msgs = dict(q.get(timeout=90) for _ in range(2))
+    for p in procs:
+        p.join(timeout=30)
+    assert msgs[1] == "raised"
+    assert msgs[0].startswith("error"), msgs[0]
+    assert time.time() - t0 < 90
