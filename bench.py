@@ -430,8 +430,38 @@ def run_reference(args):
     }))
 
 
+def run_case(args):
+    """One kernel on one shape, `--reps` launches (for ncu captures):
+    --case decode:<shape>:<M> | prefill:<shape>:<M> | dequant:<shape>, shapes from SWEEP."""
+    import torch
+
+    import awq_b200
+    kind, shape, *rest = args.case.split(":")
+    K, N = SWEEP[shape]
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev).manual_seed(5)
+    qw, qz, s = make_layer_dev(torch, K, N, dev, gen)
+    if kind == "dequant":
+        out = torch.empty((K, N), dtype=torch.float16, device=dev)
+        for _ in range(args.reps):
+            awq_b200.dequant(qw, qz, s, GS, out=out)
+    else:
+        M = int(rest[0]) if rest else (1 if kind == "decode" else 2048)
+        x = torch.randn((M, K), device=dev, generator=gen).half()
+        out = torch.empty((M, N), dtype=torch.float16, device=dev)
+        path = awq_b200.AWQ_PATH_DECODE if kind == "decode" else awq_b200.AWQ_PATH_TC
+        for _ in range(args.reps):
+            awq_b200.gemm(x, qw, qz, s, GS, path=path, out=out)
+    torch.cuda.synchronize()
+    st = awq_b200.device_status()
+    print(json.dumps({"case": args.case, "reps": args.reps, "status": st}))
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--case", default=None,
+                    help="profile one kernel: decode:<shape>:<M>, prefill:<shape>:<M>, dequant:<shape>")
+    ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
@@ -440,7 +470,9 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.case:
+        run_case(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
