@@ -41,9 +41,10 @@ namespace {
 
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-constexpr int kStages = 8;                 // per-warp ring depth (1 KB stages)
+constexpr int kStages = 4;                 // per-warp ring depth
+constexpr int kRowsPerStage = 16;          // two 8-row blocks per TMA copy
 constexpr int kStripN = 256;
-constexpr uint32_t kStageBytes = 1024;
+constexpr uint32_t kStageBytes = kRowsPerStage * 128;                // 2 KB
 constexpr uint32_t kRingBytes = kWarps * kStages * kStageBytes;   // 64 KB
 constexpr int kRedStride = 264;
 
@@ -56,7 +57,7 @@ struct TmaGemvArgs {
   int64_t ldo;
   int M, N, K, gs, PN, KB;
   int cs;          // CTAs per cluster (split-K factor)
-  int bps;         // 8-row blocks per CTA
+  int bps;         // 8-row blocks per CTA (even)
   int xs_stride;   // halves per token row of xs
   int* status;
 };
@@ -94,11 +95,27 @@ __device__ __forceinline__ float ld_dsmem_f32(uint32_t local_addr, uint32_t rank
   return v;
 }
 
+// Biased unpack: 4 half2 holding (1024 + w) for nibbles at bits 0..3 / 16..19 and
+// (1024 + 16 w) for bits 4..7 / 20..23, of the word and of word >> 8 -- exact values,
+// element pairs (0,1), (2,3), (4,5), (6,7).  No zero subtraction per weight.
+__device__ __forceinline__ void unpack_biased(uint32_t w, uint32_t d[4]) {
+  const uint32_t w8 = w >> 8;
+  d[0] = lop3_and_or(w, kLoMask, kMagic);
+  d[1] = lop3_and_or(w, kHiMask, kMagic);
+  d[2] = lop3_and_or(w8, kLoMask, kMagic);
+  d[3] = lop3_and_or(w8, kHiMask, kMagic);
+}
+
 template <int TOKSETS>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, TOKSETS == 1 ? 2 : 1)
 gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
   constexpr int MP = 4 * TOKSETS;
-  constexpr bool SPOST = (TOKSETS == 1);
+  // BIAS (one 4-token set): the MMAs accumulate x * (1024 + w) / x * (1024 + 16 w)
+  // over one quantization group; at the group's end the exact zero term
+  // (1024 + z) * sum(x) (resp. (1024 + 16 z) * sum(x)) is removed and the fp32 scale
+  // (resp. scale / 16) applied.  For more tokens W is rounded to fp16 first exactly
+  // as the reference does, and the MMA accumulates x * W directly.
+  constexpr bool BIAS = (TOKSETS == 1);
   extern __shared__ unsigned char smem_raw[];
   const uint32_t base_raw = sm100::smem_u32(smem_raw);
   const uint32_t sbase = (base_raw + 1023u) & ~1023u;
@@ -121,10 +138,12 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
   const int cb0 = rank * a.bps;
   const int cb1 = min(a.KB, cb0 + a.bps);
   const int nb = max(0, cb1 - cb0);
-  const int per = (nb + kWarps - 1) / kWarps;
+  int per = (nb + kWarps - 1) / kWarps;
+  per += per & 1;                                    // whole stages per warp
   const int b0 = cb0 + min(nb, warp * per);
   const int b1 = cb0 + min(nb, (warp + 1) * per);
   const int nblk = b1 - b0;
+  const int nst = (nblk + 1) >> 1;                   // stages this warp consumes
   const int krow0 = cb0 * 8;
   const int Kc = nb * 8;
 
@@ -139,9 +158,9 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
   }
   __syncwarp();
   if (lane == 0) {
-    for (int i = 0; i < kStages && i < nblk; ++i) {
-      sm100::mbar_arrive_expect_tx(bars + 8 * i, kStageBytes);
-      sm100::tma_load_2d(ring + i * kStageBytes, &tmW, bars + 8 * i, strip * 32, (b0 + i) * 8);
+    for (int j = 0; j < kStages && j < nst; ++j) {
+      sm100::mbar_arrive_expect_tx(bars + 8 * j, kStageBytes);
+      sm100::tma_load_2d(ring + j * kStageBytes, &tmW, bars + 8 * j, strip * 32, (b0 + 2 * j) * 8);
     }
   }
 
@@ -167,15 +186,14 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
     for (int q = 0; q < 8; ++q)
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[s][q][i] = 0.f;
-  float pacc[SPOST ? 8 : 1][4];
+  float pacc[BIAS ? 8 : 1][4];
 #pragma unroll
-  for (int q = 0; q < (SPOST ? 8 : 1); ++q)
+  for (int q = 0; q < (BIAS ? 8 : 1); ++q)
 #pragma unroll
     for (int i = 0; i < 4; ++i) pacc[q][i] = 0.f;
 
   uint32_t zcst[4][4], scl[4][4];
-  int grp_end = -1;
-  // raw zeros / scales of the next group, loaded one group ahead
+  int grp_end = -1, seg_k0 = 0;
   uint4 pf_z = make_uint4(0, 0, 0, 0), pf_s[4];
   int pf_grp = -1;
   auto load_group = [&](int grp) {
@@ -190,98 +208,149 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
         pf_s[c] = __ldg(reinterpret_cast<const uint4*>(a.scales + (int64_t)grp * a.N + (wc0 + c) * 8));
     }
   };
-  auto flush = [&]() {
-    if constexpr (SPOST) {
+  // close the segment [seg_k0, kend) of the current group (BIAS path)
+  auto flush = [&](int kend) {
+    if constexpr (BIAS) {
+      // zeros and scales of the group being closed, read here (only the flush needs them)
+      const int grp = seg_k0 / a.gs;
+      uint4 z4 = make_uint4(0, 0, 0, 0);
+      if (wc0 < a.PN) {
+        z4 = __ldg(reinterpret_cast<const uint4*>(a.qz + (int64_t)grp * a.PN + wc0));
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint4 s4 = __ldg(reinterpret_cast<const uint4*>(a.scales + (int64_t)grp * a.N + (wc0 + c) * 8));
+          scl[c][0] = s4.x; scl[c][1] = s4.y; scl[c][2] = s4.z; scl[c][3] = s4.w;
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) scl[c][0] = scl[c][1] = scl[c][2] = scl[c][3] = 0u;
+      }
+      const uint32_t zw[4] = {z4.x, z4.y, z4.z, z4.w};
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint32_t z8 = zw[c] >> 8;
+        zcst[c][0] = lop3_and_or(zw[c], kLoMask, kMagic);
+        zcst[c][1] = lop3_and_or(zw[c], kHiMask, kMagic);
+        zcst[c][2] = lop3_and_or(z8, kLoMask, kMagic);
+        zcst[c][3] = lop3_and_or(z8, kHiMask, kMagic);
+      }
+      float part = 0.f;
+      const int u0 = (seg_k0 - krow0) >> 3, u1 = (kend - krow0) >> 3;
+      for (int u = u0 + g; u < u1; u += 8) {
+        const uint4 v = *reinterpret_cast<const uint4*>(xs + t * a.xs_stride + u * 8);
+        const uint32_t hv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __half22float2(u32_as_h2(hv[j]));
+          part += f.x + f.y;
+        }
+      }
+      part += __shfl_xor_sync(0xffffffffu, part, 4);
+      part += __shfl_xor_sync(0xffffffffu, part, 8);
+      part += __shfl_xor_sync(0xffffffffu, part, 16);    // sum(x[token t]) over the segment
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         const int c = q >> 1, jj = q & 1;
-        const float2 sa = __half22float2(u32_as_h2(scl[c][2 * jj]));
-        const float2 sb = __half22float2(u32_as_h2(scl[c][2 * jj + 1]));
-        acc[0][q][0] = fmaf(sa.x, pacc[q][0], acc[0][q][0]);
-        acc[0][q][1] = fmaf(sa.y, pacc[q][1], acc[0][q][1]);
-        acc[0][q][2] = fmaf(sb.x, pacc[q][2], acc[0][q][2]);
-        acc[0][q][3] = fmaf(sb.y, pacc[q][3], acc[0][q][3]);
+        const float2 zl = __half22float2(u32_as_h2(zcst[c][2 * jj]));       // 1024 + z
+        const float2 zh = __half22float2(u32_as_h2(zcst[c][2 * jj + 1]));   // 1024 + 16 z
+        const float2 sl = __half22float2(u32_as_h2(scl[c][2 * jj]));
+        const float2 sh = __half22float2(u32_as_h2(scl[c][2 * jj + 1]));
+        acc[0][q][0] = fmaf(sl.x, fmaf(-zl.x, part, pacc[q][0]), acc[0][q][0]);
+        acc[0][q][1] = fmaf(sl.y, fmaf(-zl.y, part, pacc[q][1]), acc[0][q][1]);
+        acc[0][q][2] = fmaf(sh.x * 0.0625f, fmaf(-zh.x, part, pacc[q][2]), acc[0][q][2]);
+        acc[0][q][3] = fmaf(sh.y * 0.0625f, fmaf(-zh.y, part, pacc[q][3]), acc[0][q][3]);
 #pragma unroll
         for (int i = 0; i < 4; ++i) pacc[q][i] = 0.f;
       }
     }
+    seg_k0 = kend;
   };
 
-  int i_fail = nblk;                    // first block whose stage never arrived
-  for (int i = 0; i < nblk; ++i) {
-    const int s = i % kStages;
-    if (!sm100::mbar_wait_bounded(bars + 8 * s, (i / kStages) & 1, a.status)) {
-      i_fail = i;
+  int j_fail = nst;                     // first stage that never arrived
+  for (int j = 0; j < nst; ++j) {
+    const int s = j % kStages;
+    if (!sm100::mbar_wait_bounded(bars + 8 * s, (j / kStages) & 1, a.status)) {
+      j_fail = j;
       break;
     }
     const uint32_t st = ring + s * kStageBytes;
-    const uint4 va = lds128(st + t * 128 + ((uint32_t)(chunk ^ t) << 4));
-    const uint4 vb = lds128(st + (t + 4) * 128 + ((uint32_t)(chunk ^ (t + 4)) << 4));
-    const int bb = b0 + i;
-    const int k0 = bb * 8;
-    if (k0 >= grp_end) {
-      if (grp_end >= 0) flush();
-      const int grp = k0 / a.gs;
-      if (grp != pf_grp) load_group(grp);           // first group of the warp's range
-      grp_end = (grp + 1) * a.gs;
-      const uint32_t zw[4] = {pf_z.x, pf_z.y, pf_z.z, pf_z.w};
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        zero_consts(zw[c], zcst[c]);
-        scl[c][0] = pf_s[c].x; scl[c][1] = pf_s[c].y; scl[c][2] = pf_s[c].z; scl[c][3] = pf_s[c].w;
-      }
-      // fetch the next group now; it has a whole group of blocks to arrive
-      if (grp_end < b1 * 8) load_group(grp + 1);
-    }
-    uint32_t bf0[TOKSETS], bf1[TOKSETS];
-    const int kl = k0 - krow0;
+    for (int h = 0; h < 2; ++h) {
+      const int bb = b0 + 2 * j + h;
+      if (bb < b1) {
+        // rows t and t+4 of block h: atom h, swizzled 16-byte chunk
+        const uint4 va = lds128(st + h * 1024 + t * 128 + ((uint32_t)(chunk ^ t) << 4));
+        const uint4 vb = lds128(st + h * 1024 + (t + 4) * 128 + ((uint32_t)(chunk ^ (t + 4)) << 4));
+        const int k0 = bb * 8;
+        if (k0 >= grp_end) {
+          if (grp_end >= 0) flush(k0);
+          const int grp = k0 / a.gs;
+          grp_end = (grp + 1) * a.gs;
+          seg_k0 = k0;
+          if constexpr (!BIAS) {
+            // fp16 W path: zeros and scales are used per weight; the next group's are
+            // fetched one group ahead
+            if (grp != pf_grp) load_group(grp);
+            const uint32_t zw[4] = {pf_z.x, pf_z.y, pf_z.z, pf_z.w};
 #pragma unroll
-    for (int s2 = 0; s2 < TOKSETS; ++s2) {
-      const int m = 4 * s2 + (g >> 1);
-      const uint32_t xa = __half_as_ushort(xs[m * a.xs_stride + kl + t]);
-      const uint32_t xb = __half_as_ushort(xs[m * a.xs_stride + kl + t + 4]);
-      bf0[s2] = (g & 1) ? (xa << 16) : xa;
-      bf1[s2] = (g & 1) ? (xb << 16) : xb;
-    }
-    const uint32_t wa[4] = {va.x, va.y, va.z, va.w};
-    const uint32_t wb[4] = {vb.x, vb.y, vb.z, vb.w};
+            for (int c = 0; c < 4; ++c) {
+              zero_consts(zw[c], zcst[c]);
+              scl[c][0] = pf_s[c].x; scl[c][1] = pf_s[c].y; scl[c][2] = pf_s[c].z; scl[c][3] = pf_s[c].w;
+            }
+            if (grp_end < b1 * 8) load_group(grp + 1);
+          }
+        }
+        uint32_t bf0[TOKSETS], bf1[TOKSETS];
+        const int kl = k0 - krow0;
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      uint32_t da[4], db[4];
-      if constexpr (SPOST) {
-        unpack_minus_zero(wa[c], zcst[c], da);
-        unpack_minus_zero(wb[c], zcst[c], db);
-      } else {
-        dequant_word(wa[c], zcst[c], scl[c], da);
-        dequant_word(wb[c], zcst[c], scl[c], db);
-      }
+        for (int s2 = 0; s2 < TOKSETS; ++s2) {
+          const int m = 4 * s2 + (g >> 1);
+          const uint32_t xa = __half_as_ushort(xs[m * a.xs_stride + kl + t]);
+          const uint32_t xb = __half_as_ushort(xs[m * a.xs_stride + kl + t + 4]);
+          bf0[s2] = (g & 1) ? (xa << 16) : xa;
+          bf1[s2] = (g & 1) ? (xb << 16) : xb;
+        }
+        const uint32_t wa[4] = {va.x, va.y, va.z, va.w};
+        const uint32_t wb[4] = {vb.x, vb.y, vb.z, vb.w};
 #pragma unroll
-      for (int jj = 0; jj < 2; ++jj) {
-        const int q = 2 * c + jj;
-        if constexpr (SPOST) {
-          mma_16816(pacc[q], da[2 * jj], da[2 * jj + 1], db[2 * jj], db[2 * jj + 1], bf0[0], bf1[0]);
-        } else {
+        for (int c = 0; c < 4; ++c) {
+          uint32_t da[4], db[4];
+          if constexpr (BIAS) {
+            unpack_biased(wa[c], da);
+            unpack_biased(wb[c], db);
+          } else {
+            dequant_word(wa[c], zcst[c], scl[c], da);
+            dequant_word(wb[c], zcst[c], scl[c], db);
+          }
 #pragma unroll
-          for (int s2 = 0; s2 < TOKSETS; ++s2)
-            mma_16816(acc[s2][q], da[2 * jj], da[2 * jj + 1], db[2 * jj], db[2 * jj + 1], bf0[s2],
-                      bf1[s2]);
+          for (int jj = 0; jj < 2; ++jj) {
+            const int q = 2 * c + jj;
+            if constexpr (BIAS) {
+              mma_16816(pacc[q], da[2 * jj], da[2 * jj + 1], db[2 * jj], db[2 * jj + 1], bf0[0], bf1[0]);
+            } else {
+#pragma unroll
+              for (int s2 = 0; s2 < TOKSETS; ++s2)
+                mma_16816(acc[s2][q], da[2 * jj], da[2 * jj + 1], db[2 * jj], db[2 * jj + 1],
+                          bf0[s2], bf1[s2]);
+            }
+          }
         }
       }
     }
-    // refill this stage with block i + kStages: every lane's reads of it have
-    // completed (their values were consumed above), so the copy may overwrite it
+    // refill this stage with stage j + kStages: every lane's reads of it have completed
+    // (their values were consumed above), so the copy may overwrite it
     __syncwarp();
-    if (lane == 0 && i + kStages < nblk) {
+    if (lane == 0 && j + kStages < nst) {
       sm100::mbar_arrive_expect_tx(bars + 8 * s, kStageBytes);
-      sm100::tma_load_2d(st, &tmW, bars + 8 * s, strip * 32, (b0 + i + kStages) * 8);
+      sm100::tma_load_2d(st, &tmW, bars + 8 * s, strip * 32, (b0 + 2 * (j + kStages)) * 8);
     }
   }
-  if (grp_end >= 0) flush();
-  if (i_fail < nblk && lane == 0) {
+  if (grp_end >= 0) flush(min(b1 * 8, grp_end));
+  if (j_fail < nst && lane == 0) {
     // a stage never arrived: wait (bounded) for the copies this warp still has in
-    // flight -- blocks [i_fail, i_fail + kStages) -- before the CTA may exit
-    for (int i = i_fail; i < nblk && i < i_fail + kStages; ++i)
-      sm100::mbar_wait_bounded(bars + 8 * (i % kStages), (i / kStages) & 1, nullptr, 50000000ull);
+    // flight -- stages [j_fail, j_fail + kStages) -- before the CTA may exit
+    for (int j = j_fail; j < nst && j < j_fail + kStages; ++j)
+      sm100::mbar_wait_bounded(bars + 8 * (j % kStages), (j / kStages) & 1, nullptr, 50000000ull);
   }
   __syncwarp();
 
@@ -291,17 +360,15 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
 #pragma unroll
       for (int s2 = 0; s2 < TOKSETS; ++s2) {
         const int m = 4 * s2 + t;
-        if (m < MP) {
 #pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            float4* dst = reinterpret_cast<float4*>(red + m * kRedStride + 32 * chunk + 4 * q);
-            if (w == 0) {
-              *dst = make_float4(acc[s2][q][0], acc[s2][q][1], acc[s2][q][2], acc[s2][q][3]);
-            } else {
-              float4 v = *dst;
-              v.x += acc[s2][q][0]; v.y += acc[s2][q][1]; v.z += acc[s2][q][2]; v.w += acc[s2][q][3];
-              *dst = v;
-            }
+        for (int q = 0; q < 8; ++q) {
+          float4* dst = reinterpret_cast<float4*>(red + m * kRedStride + 32 * chunk + 4 * q);
+          if (w == 0) {
+            *dst = make_float4(acc[s2][q][0], acc[s2][q][1], acc[s2][q][2], acc[s2][q][3]);
+          } else {
+            float4 v = *dst;
+            v.x += acc[s2][q][0]; v.y += acc[s2][q][1]; v.z += acc[s2][q][2]; v.w += acc[s2][q][3];
+            *dst = v;
           }
         }
       }
@@ -405,7 +472,7 @@ cudaError_t launch_gemv_tma(const void* x, int64_t ldx, const int32_t* qweight,
   CUtensorMap tm;
   cuuint64_t dims[2] = {(cuuint64_t)(N / 8), (cuuint64_t)K};
   cuuint64_t strides[1] = {(cuuint64_t)N / 2};
-  cuuint32_t box[2] = {32, 8};
+  cuuint32_t box[2] = {32, (cuuint32_t)kRowsPerStage};
   cuuint32_t estr[2] = {1, 1};
   if (enc(&tm, CU_TENSOR_MAP_DATA_TYPE_INT32, 2, const_cast<int32_t*>(qweight), dims, strides, box,
           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -421,6 +488,7 @@ cudaError_t launch_gemv_tma(const void* x, int64_t ldx, const int32_t* qweight,
   a.N = N; a.K = K; a.gs = group_size; a.PN = N / 8; a.KB = K / 8;
   a.cs = cs;
   a.bps = (a.KB + cs - 1) / cs;
+  a.bps += a.bps & 1;                                  // whole 16-row stages
   a.xs_stride = a.bps * 8 + 8;                        // +16 B staggers token rows
   a.status = dev_status;
   const int64_t mtot = M;
@@ -446,7 +514,8 @@ cudaError_t launch_gemv_tma(const void* x, int64_t ldx, const int32_t* qweight,
 
 size_t gemv_tma_smem_bytes(int64_t M, int64_t N, int64_t K, int num_sms, int max_cs) {
   const int cs = gemv_tma_cluster_size(M < 16 ? M : 16, N, K, num_sms, max_cs);
-  const int bps = (int)((K / 8 + cs - 1) / cs);
+  int bps = (int)((K / 8 + cs - 1) / cs);
+  bps += bps & 1;
   const int mc = M < 16 ? (int)M : 16;
   const int xs_stride = bps * 8 + 8;
   return mc <= 4 ? smem_bytes<1>(xs_stride) : (mc <= 8 ? smem_bytes<2>(xs_stride) : smem_bytes<4>(xs_stride));
