@@ -7,17 +7,19 @@
 //   warp 0      TMA producer: per 64-deep K step loads the x tile (128 x 64 fp16,
 //               128-byte swizzle), the packed weight tile (64 rows x 32 words), one
 //               row of scales (256 fp16) and one row of packed zeros (32 words)
-//               into a 3-stage shared-memory ring, completion on full[s]
-//   warps 2..5  dequant: int4 -> fp16 W tile, bit-exact (fp16 (w - z) * scale),
-//               written as the UMMA B operand in the MN-major 128-byte-swizzled
-//               canonical layout, then fence.proxy.async + arrive on deq[s];
-//               after the K loop the same warps run the epilogue
+//               into a 4-stage ring, completion on tfull[s]
+//   warps 2..9  dequant: int4 -> fp16 W tile, bit-exact (fp16 (w - z) * scale), one
+//               8-row k-group per warp, written into a separate 3-stage ring as the
+//               UMMA B operand in the MN-major 128-byte-swizzled canonical layout,
+//               then fence.proxy.async + arrive on bfull[s]; after the K loop the
+//               same warps run the epilogue
 //   warp 1      TMEM allocation (256 columns) and the single-thread MMA issue:
-//               4 x tcgen05.mma.kind::f16 (M=128, N=256, K=16) per stage, then
-//               tcgen05.commit -> empty[s] frees the stage; the last commit
-//               signals the accumulator to the epilogue
-//   epilogue    tcgen05.ld 32x32b (each warp its 32 TMEM lanes = 32 rows),
-//               fp32 -> fp16, 16-byte global stores (rows >= M / cols >= N masked)
+//               4 x tcgen05.mma.kind::f16 (M=128, N=256, K=16) per K step, then
+//               tcgen05.commit -> tempty / bempty free both rings' stages; the last
+//               commit signals the accumulator to the epilogue
+//   epilogue    tcgen05.ld 32x32b (a warp reads its TMEM lane quarter = 32 rows, the
+//               two warps of a quarter split the 256 columns), fp32 -> fp16, 16-byte
+//               global stores (rows >= M / cols >= N masked)
 //
 // Shapes it takes (tc_supported): N % 32 == 0, group_size % 64 == 0 (so a K step
 // lies in one group), ldx % 8 == 0 and 16-byte aligned pointers (TMA rules).
@@ -36,14 +38,19 @@ namespace awq {
 
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 3;
-constexpr int kThreads = 192;
+constexpr int BM = 128, BN = 256, BK = 64;
+constexpr int TSTAGES = 4;                       // TMA ring: x tile + packed W + scales + zeros
+constexpr int BSTAGES = 3;                       // dequantized B ring
+constexpr int kDeqWarps = 8;                     // one 8-row k-group of a K step each
+constexpr int kThreads = (2 + kDeqWarps) * 32;   // producer, MMA, dequant/epilogue
 constexpr uint32_t A_BYTES = BM * BK * 2;        // 16 KB
 constexpr uint32_t B_BYTES = BN * BK * 2;        // 32 KB
 constexpr uint32_t RAW_BYTES = BK * (BN / 8) * 4; // 8 KB
 constexpr uint32_t SC_BYTES = BN * 2;             // 512 B
 constexpr uint32_t ZR_BYTES = (BN / 8) * 4;       // 128 B
 constexpr uint32_t TX_BYTES = A_BYTES + RAW_BYTES + SC_BYTES + ZR_BYTES;
+constexpr uint32_t T_STAGE = 25 * 1024;           // A | RAW | SC | ZR, 1 KB aligned
+constexpr uint32_t T_RAW = A_BYTES, T_SC = T_RAW + RAW_BYTES, T_ZR = T_SC + SC_BYTES;
 // B operand (MN-major, 128-byte swizzle): atom = 64 n x 8 k (1 KB); k-groups of 8
 // are SBO = 1 KB apart, 64-wide n atoms LBO = 8 KB apart.
 constexpr uint32_t B_SBO = 1024, B_LBO = 8 * 1024;
@@ -51,13 +58,11 @@ constexpr uint32_t A_SBO = 1024;                  // K-major: 8-row groups 1 KB 
 constexpr uint32_t kIdesc = sm100::idesc_f16_f32(BM, BN, /*a_mn*/ 0, /*b_mn*/ 1);
 constexpr uint32_t TMEM_COLS = 256;
 
-constexpr uint32_t OFF_A = 0;
-constexpr uint32_t OFF_B = OFF_A + STAGES * A_BYTES;
-constexpr uint32_t OFF_RAW = OFF_B + STAGES * B_BYTES;
-constexpr uint32_t OFF_SC = OFF_RAW + STAGES * RAW_BYTES;
-constexpr uint32_t OFF_ZR = OFF_SC + STAGES * SC_BYTES;
-constexpr uint32_t OFF_BAR = OFF_ZR + STAGES * ZR_BYTES;    // full, deq, empty, accf
-constexpr uint32_t OFF_MISC = OFF_BAR + (3 * STAGES + 1) * 8;
+constexpr uint32_t OFF_T = 0;
+constexpr uint32_t OFF_B = OFF_T + TSTAGES * T_STAGE;
+constexpr uint32_t OFF_BAR = OFF_B + BSTAGES * B_BYTES;   // tfull, tempty, bfull, bempty, accf
+constexpr uint32_t NBARS = 2 * TSTAGES + 2 * BSTAGES + 1;
+constexpr uint32_t OFF_MISC = OFF_BAR + NBARS * 8;
 constexpr uint32_t SMEM_BYTES = OFF_MISC + 16 + 1024;       // + alignment slack
 
 struct TcArgs {
@@ -81,18 +86,22 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   const int tile_m = blockIdx.x, tile_n = blockIdx.y;
   const int KT = args.K / BK;
 
-  auto bar_full = [&](int s) { return sbase + OFF_BAR + 8u * s; };
-  auto bar_deq = [&](int s) { return sbase + OFF_BAR + 8u * (STAGES + s); };
-  auto bar_empty = [&](int s) { return sbase + OFF_BAR + 8u * (2 * STAGES + s); };
-  const uint32_t bar_accf = sbase + OFF_BAR + 8u * (3 * STAGES);
+  auto bar_tfull = [&](int s) { return sbase + OFF_BAR + 8u * s; };
+  auto bar_tempty = [&](int s) { return sbase + OFF_BAR + 8u * (TSTAGES + s); };
+  auto bar_bfull = [&](int s) { return sbase + OFF_BAR + 8u * (2 * TSTAGES + s); };
+  auto bar_bempty = [&](int s) { return sbase + OFF_BAR + 8u * (2 * TSTAGES + BSTAGES + s); };
+  const uint32_t bar_accf = sbase + OFF_BAR + 8u * (2 * TSTAGES + 2 * BSTAGES);
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(sgen + OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sgen + OFF_MISC + 4);
 
   if (tid == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      sm100::mbar_init(bar_full(s), 1);
-      sm100::mbar_init(bar_deq(s), 4);        // one arrive per dequant warp
-      sm100::mbar_init(bar_empty(s), 1);
+    for (int s = 0; s < TSTAGES; ++s) {
+      sm100::mbar_init(bar_tfull(s), 1);
+      sm100::mbar_init(bar_tempty(s), 1);
+    }
+    for (int s = 0; s < BSTAGES; ++s) {
+      sm100::mbar_init(bar_bfull(s), kDeqWarps);   // one arrive per dequant warp
+      sm100::mbar_init(bar_bempty(s), 1);
     }
     sm100::mbar_init(bar_accf, 1);
     sm100::fence_mbar_init();
@@ -111,87 +120,94 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   sm100::tc_fence_after();
   const uint32_t tmem_d = *tmem_slot;
 
-  int issued_mma = 0;
   if (warp == 0) {
     // ------------------------------------------------------------- TMA producer ----
     if (lane == 0) {
       int kt = 0;
       for (; kt < KT; ++kt) {
-        const int s = kt % STAGES;
-        if (kt >= STAGES &&
-            !sm100::mbar_wait_bounded(bar_empty(s), ((kt / STAGES) & 1) ^ 1, args.status)) {
+        const int s = kt % TSTAGES;
+        if (kt >= TSTAGES &&
+            !sm100::mbar_wait_bounded(bar_tempty(s), ((kt / TSTAGES) & 1) ^ 1, args.status)) {
           *abort_flag = 1;
           break;
         }
         if (*abort_flag) break;
         const int k0 = kt * BK;
         const int grp = k0 / args.gs;
-        sm100::mbar_arrive_expect_tx(bar_full(s), TX_BYTES);
-        sm100::tma_load_2d(sbase + OFF_A + s * A_BYTES, &tmA, bar_full(s), k0, tile_m * BM);
-        sm100::tma_load_2d(sbase + OFF_RAW + s * RAW_BYTES, &tmW, bar_full(s), tile_n * (BN / 8), k0);
-        sm100::tma_load_2d(sbase + OFF_SC + s * SC_BYTES, &tmS, bar_full(s), tile_n * BN, grp);
-        sm100::tma_load_2d(sbase + OFF_ZR + s * ZR_BYTES, &tmZ, bar_full(s), tile_n * (BN / 8), grp);
+        const uint32_t st = sbase + OFF_T + s * T_STAGE;
+        sm100::mbar_arrive_expect_tx(bar_tfull(s), TX_BYTES);
+        sm100::tma_load_2d(st, &tmA, bar_tfull(s), k0, tile_m * BM);
+        sm100::tma_load_2d(st + T_RAW, &tmW, bar_tfull(s), tile_n * (BN / 8), k0);
+        sm100::tma_load_2d(st + T_SC, &tmS, bar_tfull(s), tile_n * BN, grp);
+        sm100::tma_load_2d(st + T_ZR, &tmZ, bar_tfull(s), tile_n * (BN / 8), grp);
       }
-      // drain: the copies of the last (up to) STAGES steps must land before exit
-      for (int j = (kt > STAGES ? kt - STAGES : 0); j < kt; ++j)
-        sm100::mbar_wait_bounded(bar_full(j % STAGES), (j / STAGES) & 1, args.status);
+      // drain: the copies of the last (up to) TSTAGES steps must land before exit
+      for (int j = (kt > TSTAGES ? kt - TSTAGES : 0); j < kt; ++j)
+        sm100::mbar_wait_bounded(bar_tfull(j % TSTAGES), (j / TSTAGES) & 1, args.status);
     }
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------- MMA issuer ------
     if (lane == 0) {
       for (int kt = 0; kt < KT; ++kt) {
-        const int s = kt % STAGES;
-        if (!sm100::mbar_wait_bounded(bar_deq(s), (kt / STAGES) & 1, args.status)) {
+        const int ts = kt % TSTAGES, bs = kt % BSTAGES;
+        if (!sm100::mbar_wait_bounded(bar_bfull(bs), (kt / BSTAGES) & 1, args.status)) {
           *abort_flag = 1;
           break;
         }
         if (*abort_flag) break;
         sm100::tc_fence_after();
-        const uint32_t a0 = sbase + OFF_A + s * A_BYTES;
-        const uint32_t b0 = sbase + OFF_B + s * B_BYTES;
+        const uint32_t a0 = sbase + OFF_T + ts * T_STAGE;
+        const uint32_t b0 = sbase + OFF_B + bs * B_BYTES;
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk) {
           const uint64_t ad = sm100::umma_desc_sw128(a0 + kk * 32, 16, A_SBO);
           const uint64_t bd = sm100::umma_desc_sw128(b0 + kk * 2 * B_SBO, B_LBO, B_SBO);
           sm100::umma_f16(tmem_d, ad, bd, kIdesc, (kt | kk) != 0);
         }
-        sm100::umma_commit(bar_empty(s));
-        issued_mma = 1;
+        sm100::umma_commit(bar_tempty(ts));      // x tile and packed inputs consumed
+        sm100::umma_commit(bar_bempty(bs));      // dequantized B consumed
       }
-      sm100::umma_commit(bar_accf);     // arrives when every issued MMA has completed
+      sm100::umma_commit(bar_accf);              // arrives when every issued MMA has completed
     }
     __syncwarp();
   } else {
     // ------------------------------------------------------------- dequant ---------
-    const int dw = warp - 2;                 // 0..3: rows [16 dw, 16 dw + 16) of a K step
+    const int dw = warp - 2;                 // 0..7: rows [8 dw, 8 dw + 8) of a K step
     const int w = lane;                      // packed word column within the tile
-    const uint32_t bst_atom = (uint32_t)(w >> 3) * B_LBO;
+    const uint32_t bst_lane = (uint32_t)(w >> 3) * B_LBO + (uint32_t)dw * B_SBO;
     for (int kt = 0; kt < KT; ++kt) {
-      const int s = kt % STAGES;
-      if (!sm100::mbar_wait_bounded(bar_full(s), (kt / STAGES) & 1, args.status)) {
+      const int ts = kt % TSTAGES, bs = kt % BSTAGES;
+      if (!sm100::mbar_wait_bounded(bar_tfull(ts), (kt / TSTAGES) & 1, args.status)) {
+        *abort_flag = 1;
+        break;
+      }
+      if (kt >= BSTAGES &&
+          !sm100::mbar_wait_bounded(bar_bempty(bs), ((kt / BSTAGES) & 1) ^ 1, args.status)) {
         *abort_flag = 1;
         break;
       }
       if (*abort_flag) break;
-      const uint32_t* raw = reinterpret_cast<const uint32_t*>(sgen + OFF_RAW + s * RAW_BYTES);
-      const uint32_t zw = reinterpret_cast<const uint32_t*>(sgen + OFF_ZR + s * ZR_BYTES)[w];
-      const uint4 s4 = reinterpret_cast<const uint4*>(sgen + OFF_SC + s * SC_BYTES)[w];
+      const unsigned char* tst = sgen + OFF_T + ts * T_STAGE;
+      const uint32_t* raw = reinterpret_cast<const uint32_t*>(tst + T_RAW) + dw * 8 * (BN / 8);
+      const uint32_t zw = reinterpret_cast<const uint32_t*>(tst + T_ZR)[w];
+      const uint4 s4 = reinterpret_cast<const uint4*>(tst + T_SC)[w];
       uint32_t zc[4], sc[4] = {s4.x, s4.y, s4.z, s4.w};
       zero_consts(zw, zc);
-      const uint32_t bstage = sbase + OFF_B + s * B_BYTES + bst_atom;
-#pragma unroll 4
-      for (int i = 0; i < 16; ++i) {
-        const int r = dw * 16 + i;           // K row within the step
+      uint32_t wv[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) wv[i] = raw[i * (BN / 8) + w];
+      const uint32_t bstage = sbase + OFF_B + bs * B_BYTES + bst_lane;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
         uint32_t d[4];
-        dequant_word(raw[r * (BN / 8) + w], zc, sc, d);
-        const uint32_t addr = bstage + (uint32_t)(r >> 3) * B_SBO + (uint32_t)(r & 7) * 128u +
-                              ((uint32_t)((w & 7) ^ (r & 7)) << 4);
+        dequant_word(wv[i], zc, sc, d);
+        const uint32_t addr = bstage + (uint32_t)i * 128u + ((uint32_t)((w & 7) ^ i) << 4);
         sm100::st_shared_v4(addr, d[0], d[1], d[2], d[3]);
       }
       sm100::fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) sm100::mbar_arrive(bar_deq(s));
+      if (lane == 0) sm100::mbar_arrive(bar_bfull(bs));
     }
 
     // ------------------------------------------------------------- epilogue --------
@@ -199,10 +215,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     sm100::tc_fence_after();
     if (ok && !*abort_flag) {
       const int q = warp & 3;                  // TMEM lane quarter this warp may access
+      const int chalf = dw >> 2;               // columns [128 chalf, 128 chalf + 128)
       const int row = tile_m * BM + q * 32 + lane;
       const uint32_t taddr = tmem_d + ((uint32_t)(q * 32) << 16);
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = chalf * 4; c < chalf * 4 + 4; ++c) {
         uint32_t v[32];
         sm100::tmem_ld_32x32b_x32(taddr + c * 32, v);
         sm100::tmem_ld_wait();
@@ -220,7 +237,6 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       }
     }
   }
-  (void)issued_mma;
 
   sm100::tc_fence_before();
   __syncthreads();
