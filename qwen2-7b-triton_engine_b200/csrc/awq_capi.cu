@@ -180,7 +180,7 @@ int awq_gemm_f16_ex(const void* x, int64_t ldx, const int32_t* qweight, const in
 
   const int max_cs = d->max_cluster;
   if (awq::gemv_tma_supported(qweight, N, ldx, x) &&
-      awq::gemv_tma_smem_bytes(M, N, K, d->num_sms, max_cs) <= awq::kGemvTmaMaxSmem) {
+      awq::gemv_tma_smem_bytes(M, N, K, group_size, d->num_sms, max_cs) <= awq::kGemvTmaMaxSmem) {
     cudaError_t e = awq::launch_gemv_tma(x, ldx, qweight, qzeros, scales, out, ldo, (int)M, (int)N,
                                          (int)K, (int)group_size, d->num_sms, max_cs, d->status, st);
     if (e != cudaSuccess) return fail_cuda(e, "decode (TMA) kernel launch");

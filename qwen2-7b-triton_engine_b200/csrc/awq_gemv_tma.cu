@@ -59,6 +59,7 @@ struct TmaGemvArgs {
   int cs;          // CTAs per cluster (split-K factor)
   int bps;         // 8-row blocks per CTA (even)
   int xs_stride;   // halves per token row of xs
+  int ngrp_cta;    // quantization groups a CTA's K range can touch (zs / ss rows)
   int* status;
 };
 
@@ -100,10 +101,15 @@ __device__ __forceinline__ float ld_dsmem_f32(uint32_t local_addr, uint32_t rank
 // element pairs (0,1), (2,3), (4,5), (6,7).  No zero subtraction per weight.
 __device__ __forceinline__ void unpack_biased(uint32_t w, uint32_t d[4]) {
   const uint32_t w8 = w >> 8;
-  d[0] = lop3_and_or(w, kLoMask, kMagic);
-  d[1] = lop3_and_or(w, kHiMask, kMagic);
-  d[2] = lop3_and_or(w8, kLoMask, kMagic);
-  d[3] = lop3_and_or(w8, kHiMask, kMagic);
+  d[0] = lop3_and_or_imm<kLoMask, kMagic>(w);
+  d[1] = lop3_and_or_imm<kHiMask, kMagic>(w);
+  d[2] = lop3_and_or_imm<kLoMask, kMagic>(w8);
+  d[3] = lop3_and_or_imm<kHiMask, kMagic>(w8);
+}
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
 }
 
 template <int TOKSETS>
@@ -120,12 +126,16 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
   const uint32_t base_raw = sm100::smem_u32(smem_raw);
   const uint32_t sbase = (base_raw + 1023u) & ~1023u;
   unsigned char* sgen = smem_raw + (sbase - base_raw);
-  // layout: ring | red (MP x 264 fp32) | bars (kWarps x kStages) | xs
+  // layout: ring | red (MP x 264 fp32) | bars (kWarps x kStages) | xs | zs | ss
   const uint32_t off_red = kRingBytes;
   const uint32_t off_bar = off_red + MP * kRedStride * 4;
   const uint32_t off_xs = off_bar + kWarps * kStages * 8;
+  const uint32_t off_zs = off_xs + (uint32_t)MP * a.xs_stride * 2;
+  const uint32_t off_ss = off_zs + (uint32_t)a.ngrp_cta * 128;
   float* red = reinterpret_cast<float*>(sgen + off_red);
   __half* xs = reinterpret_cast<__half*>(sgen + off_xs);
+  uint32_t* zs = reinterpret_cast<uint32_t*>(sgen + off_zs);    // [group][32 words]
+  __half* ss = reinterpret_cast<__half*>(sgen + off_ss);        // [group][256]
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -150,12 +160,18 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
   const uint32_t ring = sbase + (uint32_t)warp * kStages * kStageBytes;
   const uint32_t bars = sbase + off_bar + (uint32_t)warp * kStages * 8;
 
-  // ---- barriers, then start streaming before anything else -------------------------
+  // ---- barriers, L2 prefetch of the first tiles, then wait for the previous grid -----
+  // Under programmatic dependent launch this prologue overlaps the tail of the
+  // preceding kernel; nothing below griddepcontrol.wait reads memory it may write.
   if (lane == 0) {
     for (int s = 0; s < kStages; ++s) sm100::mbar_init(bars + 8 * s, 1);
     sm100::fence_mbar_init();
     sm100::prefetch_tmap(&tmW);
+    for (int j = 0; j < 2 * kStages && j < nst; ++j)
+      sm100::tma_prefetch_l2_2d(&tmW, strip * 32, (b0 + 2 * j) * 8);
   }
+  sm100::grid_dependency_wait();
+  sm100::grid_launch_dependents();
   __syncwarp();
   if (lane == 0) {
     for (int j = 0; j < kStages && j < nst; ++j) {
@@ -174,10 +190,30 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
         val = __ldg(reinterpret_cast<const uint4*>(a.x + (int64_t)(m0 + m) * a.ldx + krow0) + v);
       *reinterpret_cast<uint4*>(xs + m * a.xs_stride + v * 8) = val;
     }
+    // zeros (32 words) and scales (256 fp16) of the strip for the CTA's groups
+    const int g0 = krow0 / a.gs;
+    const int ng = Kc > 0 ? (krow0 + Kc - 1) / a.gs - g0 + 1 : 0;
+    for (int i = tid; i < ng * 40; i += kThreads) {
+      const int gi = i / 40, v = i - gi * 40;     // 8 vectors of zeros, 32 of scales
+      uint4 val = make_uint4(0, 0, 0, 0);
+      if (v < 8) {
+        const int wc = strip * 32 + v * 4;
+        if (wc < a.PN) val = __ldg(reinterpret_cast<const uint4*>(a.qz + (int64_t)(g0 + gi) * a.PN + wc));
+        reinterpret_cast<uint4*>(zs + gi * 32)[v] = val;
+      } else {
+        const int n = strip * kStripN + (v - 8) * 8;
+        if (n < a.N) val = __ldg(reinterpret_cast<const uint4*>(a.scales + (int64_t)(g0 + gi) * a.N + n));
+        reinterpret_cast<uint4*>(ss + gi * kStripN)[v - 8] = val;
+      }
+    }
   }
   __syncthreads();
+  const int grp0 = krow0 / a.gs;                      // first group staged in zs / ss
 
   const int chunk = (g >> 1) | ((g & 1) << 2);       // conflict-free word chunk
+  // B column g = (token g/2, pair slot g%2): x goes to the low half for slot 0 and
+  // to the high half for slot 1 (prmt selector; bytes 4..7 come from the zero word)
+  const uint32_t bsel = (g & 1) ? 0x1054u : 0x5410u;
   const int wc0 = strip * 32 + chunk * 4;            // first packed word of this lane
   float acc[TOKSETS][8][4];
 #pragma unroll
@@ -194,36 +230,16 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
 
   uint32_t zcst[4][4], scl[4][4];
   int grp_end = -1, seg_k0 = 0;
-  uint4 pf_z = make_uint4(0, 0, 0, 0), pf_s[4];
-  int pf_grp = -1;
-  auto load_group = [&](int grp) {
-    pf_grp = grp;
-    pf_z = make_uint4(0, 0, 0, 0);
-#pragma unroll
-    for (int c = 0; c < 4; ++c) pf_s[c] = make_uint4(0, 0, 0, 0);
-    if (wc0 < a.PN) {
-      pf_z = __ldg(reinterpret_cast<const uint4*>(a.qz + (int64_t)grp * a.PN + wc0));
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-        pf_s[c] = __ldg(reinterpret_cast<const uint4*>(a.scales + (int64_t)grp * a.N + (wc0 + c) * 8));
-    }
-  };
   // close the segment [seg_k0, kend) of the current group (BIAS path)
   auto flush = [&](int kend) {
     if constexpr (BIAS) {
-      // zeros and scales of the group being closed, read here (only the flush needs them)
-      const int grp = seg_k0 / a.gs;
-      uint4 z4 = make_uint4(0, 0, 0, 0);
-      if (wc0 < a.PN) {
-        z4 = __ldg(reinterpret_cast<const uint4*>(a.qz + (int64_t)grp * a.PN + wc0));
+      // zeros and scales of the group being closed, from the CTA's shared-memory copy
+      const int gl = seg_k0 / a.gs - grp0;
+      const uint4 z4 = reinterpret_cast<const uint4*>(zs + gl * 32)[chunk];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const uint4 s4 = __ldg(reinterpret_cast<const uint4*>(a.scales + (int64_t)grp * a.N + (wc0 + c) * 8));
-          scl[c][0] = s4.x; scl[c][1] = s4.y; scl[c][2] = s4.z; scl[c][3] = s4.w;
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < 4; ++c) scl[c][0] = scl[c][1] = scl[c][2] = scl[c][3] = 0u;
+      for (int c = 0; c < 4; ++c) {
+        const uint4 s4 = reinterpret_cast<const uint4*>(ss + gl * kStripN)[chunk * 4 + c];
+        scl[c][0] = s4.x; scl[c][1] = s4.y; scl[c][2] = s4.z; scl[c][3] = s4.w;
       }
       const uint32_t zw[4] = {z4.x, z4.y, z4.z, z4.w};
 #pragma unroll
@@ -288,27 +304,27 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
           grp_end = (grp + 1) * a.gs;
           seg_k0 = k0;
           if constexpr (!BIAS) {
-            // fp16 W path: zeros and scales are used per weight; the next group's are
-            // fetched one group ahead
-            if (grp != pf_grp) load_group(grp);
-            const uint32_t zw[4] = {pf_z.x, pf_z.y, pf_z.z, pf_z.w};
+            // fp16 W path: zeros and scales are used per weight
+            const int gl = grp - grp0;
+            const uint4 z4 = reinterpret_cast<const uint4*>(zs + gl * 32)[chunk];
+            const uint32_t zw[4] = {z4.x, z4.y, z4.z, z4.w};
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
               zero_consts(zw[c], zcst[c]);
-              scl[c][0] = pf_s[c].x; scl[c][1] = pf_s[c].y; scl[c][2] = pf_s[c].z; scl[c][3] = pf_s[c].w;
+              const uint4 s4 = reinterpret_cast<const uint4*>(ss + gl * kStripN)[chunk * 4 + c];
+              scl[c][0] = s4.x; scl[c][1] = s4.y; scl[c][2] = s4.z; scl[c][3] = s4.w;
             }
-            if (grp_end < b1 * 8) load_group(grp + 1);
           }
         }
         uint32_t bf0[TOKSETS], bf1[TOKSETS];
         const int kl = k0 - krow0;
 #pragma unroll
         for (int s2 = 0; s2 < TOKSETS; ++s2) {
-          const int m = 4 * s2 + (g >> 1);
-          const uint32_t xa = __half_as_ushort(xs[m * a.xs_stride + kl + t]);
-          const uint32_t xb = __half_as_ushort(xs[m * a.xs_stride + kl + t + 4]);
-          bf0[s2] = (g & 1) ? (xa << 16) : xa;
-          bf1[s2] = (g & 1) ? (xb << 16) : xb;
+          const __half* xp = xs + (4 * s2 + (g >> 1)) * a.xs_stride + kl + t;
+          const uint32_t xa = __half_as_ushort(xp[0]);
+          const uint32_t xb = __half_as_ushort(xp[4]);
+          bf0[s2] = prmt(xa, 0u, bsel);          // x in the slot of this lane's column
+          bf1[s2] = prmt(xb, 0u, bsel);
         }
         const uint32_t wa[4] = {va.x, va.y, va.z, va.w};
         const uint32_t wb[4] = {vb.x, vb.y, vb.z, vb.w};
@@ -412,10 +428,10 @@ EncodeTiledFn encode_fn() {
 }
 
 template <int TOKSETS>
-size_t smem_bytes(int xs_stride) {
+size_t smem_bytes(int xs_stride, int ngrp) {
   const int MP = 4 * TOKSETS;
   return 1024 + kRingBytes + (size_t)MP * kRedStride * 4 + kWarps * kStages * 8 +
-         (size_t)MP * xs_stride * 2;
+         (size_t)MP * xs_stride * 2 + (size_t)ngrp * (128 + kStripN * 2);
 }
 
 template <int TOKSETS>
@@ -436,13 +452,17 @@ cudaError_t launch_t(const CUtensorMap& tm, const TmaGemvArgs& a, int strips, in
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute at[1];
+  cudaLaunchAttribute at[2];
   at[0].id = cudaLaunchAttributeClusterDimension;
   at[0].val.clusterDim.x = a.cs;
   at[0].val.clusterDim.y = 1;
   at[0].val.clusterDim.z = 1;
+  // programmatic dependent launch: the kernel waits (griddepcontrol.wait) before it
+  // touches anything the previous grid may write
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, gemv_tma_kernel<TOKSETS>, tm, a);
 }
 
@@ -490,6 +510,7 @@ cudaError_t launch_gemv_tma(const void* x, int64_t ldx, const int32_t* qweight,
   a.bps = (a.KB + cs - 1) / cs;
   a.bps += a.bps & 1;                                  // whole 16-row stages
   a.xs_stride = a.bps * 8 + 8;                        // +16 B staggers token rows
+  a.ngrp_cta = (a.bps * 8 + group_size - 1) / group_size + 1;
   a.status = dev_status;
   const int64_t mtot = M;
   const int mc = M < 16 ? M : 16;
@@ -503,22 +524,25 @@ cudaError_t launch_gemv_tma(const void* x, int64_t ldx, const int32_t* qweight,
     const int z = (int)((rows + 15) / 16);
     cudaError_t e;
     switch (toksets) {
-      case 1: e = launch_t<1>(tm, a, strips, z, smem_bytes<1>(a.xs_stride), stream); break;
-      case 2: e = launch_t<2>(tm, a, strips, z, smem_bytes<2>(a.xs_stride), stream); break;
-      default: e = launch_t<4>(tm, a, strips, z, smem_bytes<4>(a.xs_stride), stream); break;
+      case 1: e = launch_t<1>(tm, a, strips, z, smem_bytes<1>(a.xs_stride, a.ngrp_cta), stream); break;
+      case 2: e = launch_t<2>(tm, a, strips, z, smem_bytes<2>(a.xs_stride, a.ngrp_cta), stream); break;
+      default: e = launch_t<4>(tm, a, strips, z, smem_bytes<4>(a.xs_stride, a.ngrp_cta), stream); break;
     }
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
 }
 
-size_t gemv_tma_smem_bytes(int64_t M, int64_t N, int64_t K, int num_sms, int max_cs) {
+size_t gemv_tma_smem_bytes(int64_t M, int64_t N, int64_t K, int64_t group_size, int num_sms,
+                           int max_cs) {
   const int cs = gemv_tma_cluster_size(M < 16 ? M : 16, N, K, num_sms, max_cs);
   int bps = (int)((K / 8 + cs - 1) / cs);
   bps += bps & 1;
   const int mc = M < 16 ? (int)M : 16;
   const int xs_stride = bps * 8 + 8;
-  return mc <= 4 ? smem_bytes<1>(xs_stride) : (mc <= 8 ? smem_bytes<2>(xs_stride) : smem_bytes<4>(xs_stride));
+  const int ngrp = (int)((bps * 8 + group_size - 1) / group_size) + 1;
+  return mc <= 4 ? smem_bytes<1>(xs_stride, ngrp)
+                 : (mc <= 8 ? smem_bytes<2>(xs_stride, ngrp) : smem_bytes<4>(xs_stride, ngrp));
 }
 
 }  // namespace awq

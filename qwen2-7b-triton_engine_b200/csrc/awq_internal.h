@@ -37,7 +37,8 @@ cudaError_t launch_gemv(const GemvPlan& plan, const void* x, int64_t ldx, const 
 // ---- decode on mma.sync with TMA streaming and cluster split-K (awq_gemv_tma.cu) -------
 // Shapes TMA can describe (N % 32 == 0, 16-byte aligned qweight and x, ldx % 8 == 0).
 bool gemv_tma_supported(const int32_t* qweight, int64_t N, int64_t ldx, const void* x);
-size_t gemv_tma_smem_bytes(int64_t M, int64_t N, int64_t K, int num_sms, int max_cs);
+size_t gemv_tma_smem_bytes(int64_t M, int64_t N, int64_t K, int64_t group_size, int num_sms,
+                           int max_cs);
 int gemv_tma_cluster_size(int64_t M, int64_t N, int64_t K, int num_sms, int max_cs);
 cudaError_t launch_gemv_tma(const void* x, int64_t ldx, const int32_t* qweight,
                             const int32_t* qzeros, const void* scales, void* out, int64_t ldo,
