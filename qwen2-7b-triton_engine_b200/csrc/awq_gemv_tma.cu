@@ -29,6 +29,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "awq_common.cuh"
@@ -101,10 +102,10 @@ __device__ __forceinline__ float ld_dsmem_f32(uint32_t local_addr, uint32_t rank
 // element pairs (0,1), (2,3), (4,5), (6,7).  No zero subtraction per weight.
 __device__ __forceinline__ void unpack_biased(uint32_t w, uint32_t d[4]) {
   const uint32_t w8 = w >> 8;
-  d[0] = lop3_and_or_imm<kLoMask, kMagic>(w);
-  d[1] = lop3_and_or_imm<kHiMask, kMagic>(w);
-  d[2] = lop3_and_or_imm<kLoMask, kMagic>(w8);
-  d[3] = lop3_and_or_imm<kHiMask, kMagic>(w8);
+  d[0] = lop3_and_or(w, kLoMask, kMagic);
+  d[1] = lop3_and_or(w, kHiMask, kMagic);
+  d[2] = lop3_and_or(w8, kLoMask, kMagic);
+  d[3] = lop3_and_or(w8, kHiMask, kMagic);
 }
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   uint32_t r;
@@ -434,6 +435,16 @@ size_t smem_bytes(int xs_stride, int ngrp) {
          (size_t)MP * xs_stride * 2 + (size_t)ngrp * (128 + kStripN * 2);
 }
 
+// Programmatic dependent launch is on unless AWQ_PDL=0 (read once per process).
+bool pdl_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("AWQ_PDL");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
 template <int TOKSETS>
 cudaError_t launch_t(const CUtensorMap& tm, const TmaGemvArgs& a, int strips, int zchunks,
                      size_t smem, cudaStream_t stream) {
@@ -462,7 +473,7 @@ cudaError_t launch_t(const CUtensorMap& tm, const TmaGemvArgs& a, int strips, in
   at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   at[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
-  cfg.numAttrs = 2;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, gemv_tma_kernel<TOKSETS>, tm, a);
 }
 
