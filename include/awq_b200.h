@@ -90,6 +90,26 @@ AWQ_API int awq_gemm_f16_ex(const void* x, int64_t ldx, const int32_t* qweight, 
                     int64_t group_size, void* workspace, size_t workspace_bytes, void* stream,
                     int path);
 
+/*
+ * awq_gemm_f16 for callers that cannot allocate device memory: same inputs and
+ * output, no workspace argument.  No counterpart in the reference (its M<=4 path
+ * allocates a global K*N buffer, kernels/awq_gemm.py:255-262).  Meant for hosts that
+ * forbid allocation on the path where the product runs -- an engine that plans all
+ * device memory up front (cudaMalloc / cudaFree can synchronize the device), or a
+ * plugin interface that hands the library only its input and output buffers.
+ *   - Runs the generic decode kernel (any M, 16-row chunks; fastest for M <= 16).
+ *   - Its split-K scratch is a 4 MiB file-scope device array, held by every GPU that
+ *     loads the library until the process exits.  The split factor is reduced until the
+ *     partial sums fit; a shape that still does not fit returns AWQ_ERR_WORKSPACE.
+ *   - The first call on a device looks up the array's address and zero-fills its
+ *     counters (synchronous cudaMemset): make it before any stream capture.
+ *   - All calls share the array: calls that overlap on the GPU race and give wrong
+ *     results.  No allocation of any kind happens inside.
+ */
+AWQ_API int awq_gemm_f16_noalloc(const void* x, int64_t ldx, const int32_t* qweight,
+                                 const int32_t* qzeros, const void* scales, void* out, int64_t ldo,
+                                 int64_t M, int64_t N, int64_t K, int64_t group_size, void* stream);
+
 /* 1 if AWQ_PATH_TC can run this shape with these pointers, else 0. */
 AWQ_API int awq_tc_supported(const void* x, int64_t ldx, const int32_t* qweight, const int32_t* qzeros,
                      const void* scales, int64_t M, int64_t N, int64_t K, int64_t group_size);

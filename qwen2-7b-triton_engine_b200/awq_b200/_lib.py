@@ -38,6 +38,7 @@ SIGNATURES = {
     "awq_gemm_f16": ([_P, _I64, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _SZ, _P], _INT),
     "awq_gemm_f16_ex": ([_P, _I64, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _SZ, _P,
                          _INT], _INT),
+    "awq_gemm_f16_noalloc": ([_P, _I64, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P], _INT),
     "awq_tc_supported": ([_P, _I64, _P, _P, _P, _I64, _I64, _I64, _I64], _INT),
     "awq_device_status": ([_P, ctypes.POINTER(ctypes.c_int)], _INT),
 }

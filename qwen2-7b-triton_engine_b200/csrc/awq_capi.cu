@@ -100,6 +100,11 @@ int check_weights(const int32_t* qweight, const int32_t* qzeros, const void* sca
 
 }  // namespace
 
+int awq::set_last_error(int code, const char* msg) {
+  g_last_error = msg;
+  return code;
+}
+
 extern "C" {
 
 int awq_version(void) { return 100; }

@@ -345,6 +345,38 @@ bool plan_gemv(int64_t M, int64_t N, int64_t K, int64_t group_size, int num_sms,
   return true;
 }
 
+bool plan_gemv_bounded(int64_t M, int64_t N, int64_t K, int64_t group_size, int num_sms,
+                       bool vec_ok, size_t max_workspace, GemvPlan* plan) {
+  GemvPlan p;
+  if (!plan_gemv(M, N, K, group_size, num_sms, vec_ok, &p)) return false;
+  // fewer splits -> smaller partial buffer; the shared-memory bound sets the floor
+  const int64_t KB = K / 8;
+  const int MP = 4 * p.toksets;
+  const size_t NP = (size_t)p.strips * kStripN;
+  int64_t splits = p.splits;
+  for (;;) {
+    int64_t bps = (KB + splits - 1) / splits;
+    int64_t sp = (KB + bps - 1) / bps;
+    size_t xs_bytes = (size_t)bps * 8 * MP * sizeof(uint16_t);
+    size_t red_bytes = (size_t)MP * kRedStride * sizeof(float);
+    size_t smem = xs_bytes > red_bytes ? xs_bytes : red_bytes;
+    size_t partials = sp > 1 ? (size_t)p.zchunks * sp * 16 * NP * sizeof(float) : 0;
+    size_t need = sp > 1 ? kCounterRegionBytes + align_up(partials, 256) : 0;
+    if (smem > 48 * 1024) return false;               // cannot shrink further
+    if (need <= max_workspace) {
+      p.bps = (int)bps;
+      p.splits = (int)sp;
+      p.smem = smem;
+      p.ws_partials_bytes = partials;
+      break;
+    }
+    if (sp <= 1) return false;
+    splits = sp / 2;
+  }
+  *plan = p;
+  return true;
+}
+
 size_t gemv_workspace_bytes(const GemvPlan& plan) {
   if (plan.splits <= 1) return 0;
   return kCounterRegionBytes + align_up(plan.ws_partials_bytes, 256);

@@ -30,6 +30,10 @@ struct GemvPlan {
 bool plan_gemv(int64_t M, int64_t N, int64_t K, int64_t group_size, int num_sms, bool vec_ok,
                GemvPlan* plan);
 size_t gemv_workspace_bytes(const GemvPlan& plan);
+// plan_gemv with the split-K factor reduced until the workspace fits `max_workspace`
+// bytes; false if even the smallest plan does not fit.
+bool plan_gemv_bounded(int64_t M, int64_t N, int64_t K, int64_t group_size, int num_sms,
+                       bool vec_ok, size_t max_workspace, GemvPlan* plan);
 cudaError_t launch_gemv(const GemvPlan& plan, const void* x, int64_t ldx, const int32_t* qweight,
                         const int32_t* qzeros, const void* scales, void* out, int64_t ldo, int M,
                         int N, int K, int group_size, void* workspace, cudaStream_t stream);
@@ -54,5 +58,8 @@ cudaError_t launch_gemm_tc(const void* x, int64_t ldx, const int32_t* qweight,
                            const int32_t* qzeros, const void* scales, void* out, int64_t ldo,
                            int M, int N, int K, int group_size, int num_sms, int* dev_status,
                            cudaStream_t stream, const char** why);
+
+// Sets the message awq_last_error() returns on this thread; returns `code`.
+int set_last_error(int code, const char* msg);
 
 }  // namespace awq
