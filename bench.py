@@ -130,15 +130,6 @@ def make_layer_dev(torch, K, N, dev, gen):
     return qw, qz, s
 
 
-def shard_cols(t_qw, t_qz, t_s, rank, world):
-    """Column shard (split N) of one packed layer, in whole packed words."""
-    N = t_s.shape[1]
-    n = N // world
-    return (t_qw[:, rank * n // 8:(rank + 1) * n // 8].contiguous(),
-            t_qz[:, rank * n // 8:(rank + 1) * n // 8].contiguous(),
-            t_s[:, rank * n:(rank + 1) * n].contiguous())
-
-
 def cpu_baseline(torch, sample_seconds=12.0):
     """Reference host path (oracle port) on one layer's 4 linears at M=1."""
     from oracle import oracle as O
@@ -174,6 +165,7 @@ def run_ours(args):
     import torch.distributed as dist
 
     import awq_b200
+    from awq_b200 import tp
     from kernels import awq_gemm
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -196,15 +188,16 @@ def run_ours(args):
             full_bytes += alg_bytes(1, K, N)
             if world == 1:
                 calls.append((name, K, N, make_layer_dev(torch, K, N, dev, gen), False))
-            elif name in ("qkv", "gate_up"):            # column parallel
-                calls.append((name, K, N // world, make_layer_dev(torch, K, N // world, dev, gen),
-                               False))
-            else:                                       # row parallel + all-reduce
-                kl = K // world
-                kl -= kl % GS
-                if rank == world - 1:
-                    kl = K - kl * (world - 1)
-                calls.append((name, kl, N, make_layer_dev(torch, kl, N, dev, gen), True))
+            elif name == "qkv":                          # column parallel, whole words
+                n0, n1 = tp.column_bounds(N, world, rank)
+                calls.append((name, K, n1 - n0, make_layer_dev(torch, K, n1 - n0, dev, gen), False))
+            elif name == "gate_up":                      # gate and up split in whole groups
+                i0, i1 = tp.row_bounds(INTER, GS, world, rank)
+                nl = 2 * (i1 - i0)
+                calls.append((name, K, nl, make_layer_dev(torch, K, nl, dev, gen), False))
+            else:                                        # row parallel + all-reduce
+                k0, k1 = tp.row_bounds(K, GS, world, rank)
+                calls.append((name, k1 - k0, N, make_layer_dev(torch, k1 - k0, N, dev, gen), True))
     xs = {}
     for name, K, N, _, _ in calls:
         xs.setdefault(K, torch.randn((1, K), device=dev, generator=gen).half())
@@ -288,30 +281,39 @@ def run_ours(args):
         result["clocks"] = clk.summary()
 
     # ---- end to end through the public drop-in, host buffers ------------------------
-    if world == 1:
-        hx = [torch.randn((1, K)).half().pin_memory() for (_, K, _, _, _) in calls]
-        hout = [torch.empty((1, N), dtype=torch.float16).pin_memory() for (_, _, N, _, _) in calls]
-        dx = [torch.empty((1, K), dtype=torch.float16, device=dev) for (_, K, _, _, _) in calls]
+    hx = [torch.randn((1, K)).half().pin_memory() for (_, K, _, _, _) in calls]
+    hout = [torch.empty((1, N), dtype=torch.float16).pin_memory() for (_, _, N, _, _) in calls]
+    dx = [torch.empty((1, K), dtype=torch.float16, device=dev) for (_, K, _, _, _) in calls]
 
-        def e2e_step():
-            for i, (name, K, N, (qw, qz, s), _) in enumerate(calls):
-                dx[i].copy_(hx[i], non_blocking=True)
-                y = awq_gemm.awq_gemm_forward(dx[i], qw, qz, s, GS)
-                hout[i].copy_(y, non_blocking=True)
-            torch.cuda.synchronize()
-        for _ in range(max(1, args.warmup)):
-            e2e_step()
-        e2e_steps = max(3, min(args.steps, 20))
-        t0 = time.perf_counter()
-        for _ in range(e2e_steps):
-            e2e_step()
-        e2e_ms = (time.perf_counter() - t0) * 1e3 / e2e_steps
+    def e2e_step():
+        for i, (name, K, N, (qw, qz, s), red) in enumerate(calls):
+            dx[i].copy_(hx[i], non_blocking=True)
+            y = awq_gemm.awq_gemm_forward(dx[i], qw, qz, s, GS)
+            if red:
+                dist.all_reduce(y)
+            hout[i].copy_(y, non_blocking=True)
+        torch.cuda.synchronize()
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    e2e_steps = max(3, min(args.steps, 20))
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e2e_ms = (time.perf_counter() - t0) * 1e3 / e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    if rank == 0:
         result["e2e"] = {"value": round(full_bytes / (e2e_ms * 1e-3) / 1e12, 4), "unit": "TB/s",
                          "ms_per_step": round(e2e_ms, 4),
                          "h2d_bytes_per_step": sum(2 * K for (_, K, _, _, _) in calls),
                          "d2h_bytes_per_step": sum(2 * N for (_, _, N, _, _) in calls),
-                         "api": "kernels.awq_gemm.awq_gemm_forward (eager, 112 calls)"}
-        result["gpu_launches"] += 0
+                         "api": "kernels.awq_gemm.awq_gemm_forward (eager, 112 calls"
+                                + (", NCCL all-reduce after o and down)" if world > 1 else ")")}
+    if world == 1:
         result["prefill"] = prefill_bench(torch, awq_b200, dev, tc_peak, peak_src, args)
         result["sweep"] = decode_sweep(torch, lib, awq_b200, dev, hbm_peak)
         result["cpu_baseline"] = cpu_baseline(torch, args.cpu_seconds)

@@ -38,32 +38,39 @@ namespace awq {
 
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 64;
-constexpr int TSTAGES = 4;                       // TMA ring: x tile + packed W + scales + zeros
-constexpr int BSTAGES = 3;                       // dequantized B ring
+constexpr int BN = 256, BK = 64;
 constexpr int kDeqWarps = 8;                     // one 8-row k-group of a K step each
 constexpr int kThreads = (2 + kDeqWarps) * 32;   // producer, MMA, dequant/epilogue
-constexpr uint32_t A_BYTES = BM * BK * 2;        // 16 KB
 constexpr uint32_t B_BYTES = BN * BK * 2;        // 32 KB
 constexpr uint32_t RAW_BYTES = BK * (BN / 8) * 4; // 8 KB
 constexpr uint32_t SC_BYTES = BN * 2;             // 512 B
 constexpr uint32_t ZR_BYTES = (BN / 8) * 4;       // 128 B
-constexpr uint32_t TX_BYTES = A_BYTES + RAW_BYTES + SC_BYTES + ZR_BYTES;
-constexpr uint32_t T_STAGE = 25 * 1024;           // A | RAW | SC | ZR, 1 KB aligned
-constexpr uint32_t T_RAW = A_BYTES, T_SC = T_RAW + RAW_BYTES, T_ZR = T_SC + SC_BYTES;
 // B operand (MN-major, 128-byte swizzle): atom = 64 n x 8 k (1 KB); k-groups of 8
 // are SBO = 1 KB apart, 64-wide n atoms LBO = 8 KB apart.
 constexpr uint32_t B_SBO = 1024, B_LBO = 8 * 1024;
 constexpr uint32_t A_SBO = 1024;                  // K-major: 8-row groups 1 KB apart
-constexpr uint32_t kIdesc = sm100::idesc_f16_f32(BM, BN, /*a_mn*/ 0, /*b_mn*/ 1);
-constexpr uint32_t TMEM_COLS = 256;
+constexpr uint32_t kIdesc = sm100::idesc_f16_f32(128, BN, /*a_mn*/ 0, /*b_mn*/ 1);
 
-constexpr uint32_t OFF_T = 0;
-constexpr uint32_t OFF_B = OFF_T + TSTAGES * T_STAGE;
-constexpr uint32_t OFF_BAR = OFF_B + BSTAGES * B_BYTES;   // tfull, tempty, bfull, bempty, accf
-constexpr uint32_t NBARS = 2 * TSTAGES + 2 * BSTAGES + 1;
-constexpr uint32_t OFF_MISC = OFF_BAR + NBARS * 8;
-constexpr uint32_t SMEM_BYTES = OFF_MISC + 16 + 1024;       // + alignment slack
+// Tile geometry for NACC accumulators of 128 x 256 (BM = 128 * NACC rows per CTA).  Each
+// dequantized B tile feeds NACC MMAs, so the dequant work per tensor flop falls as
+// 1 / NACC.
+template <int NACC>
+struct Geo {
+  static constexpr int BM = 128 * NACC;
+  static constexpr int TSTAGES = NACC == 1 ? 4 : 3;   // TMA ring depth
+  static constexpr int BSTAGES = NACC == 1 ? 3 : 2;   // dequantized B ring depth
+  static constexpr uint32_t A_BYTES = BM * BK * 2;
+  static constexpr uint32_t TX_BYTES = A_BYTES + RAW_BYTES + SC_BYTES + ZR_BYTES;
+  static constexpr uint32_t T_RAW = A_BYTES, T_SC = T_RAW + RAW_BYTES, T_ZR = T_SC + SC_BYTES;
+  static constexpr uint32_t T_STAGE = (T_ZR + ZR_BYTES + 1023) / 1024 * 1024;
+  static constexpr uint32_t OFF_T = 0;
+  static constexpr uint32_t OFF_B = OFF_T + TSTAGES * T_STAGE;
+  static constexpr uint32_t OFF_BAR = OFF_B + BSTAGES * B_BYTES;  // tfull, tempty, bfull, bempty, accf
+  static constexpr uint32_t NBARS = 2 * TSTAGES + 2 * BSTAGES + 1;
+  static constexpr uint32_t OFF_MISC = OFF_BAR + NBARS * 8;
+  static constexpr uint32_t SMEM_BYTES = OFF_MISC + 16 + 1024;      // + alignment slack
+  static constexpr uint32_t TMEM_COLS = 256 * NACC;
+};
 
 struct TcArgs {
   __half* out;
@@ -72,10 +79,16 @@ struct TcArgs {
   int* status;
 };
 
+template <int NACC>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmZ,
                const TcArgs args) {
+  using G = Geo<NACC>;
+  constexpr int BM = G::BM, TSTAGES = G::TSTAGES, BSTAGES = G::BSTAGES;
+  constexpr uint32_t T_STAGE = G::T_STAGE, T_RAW = G::T_RAW, T_SC = G::T_SC, T_ZR = G::T_ZR;
+  constexpr uint32_t OFF_T = G::OFF_T, OFF_B = G::OFF_B, OFF_BAR = G::OFF_BAR, OFF_MISC = G::OFF_MISC;
+  constexpr uint32_t TX_BYTES = G::TX_BYTES, TMEM_COLS = G::TMEM_COLS;
   extern __shared__ unsigned char smem_raw[];
   const uint32_t base_raw = sm100::smem_u32(smem_raw);
   const uint32_t sbase = (base_raw + 1023u) & ~1023u;        // 1 KB aligned (swizzle atoms)
@@ -161,9 +174,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const uint32_t b0 = sbase + OFF_B + bs * B_BYTES;
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk) {
-          const uint64_t ad = sm100::umma_desc_sw128(a0 + kk * 32, 16, A_SBO);
           const uint64_t bd = sm100::umma_desc_sw128(b0 + kk * 2 * B_SBO, B_LBO, B_SBO);
-          sm100::umma_f16(tmem_d, ad, bd, kIdesc, (kt | kk) != 0);
+#pragma unroll
+          for (int h = 0; h < NACC; ++h) {     // rows [128 h, 128 h + 128) -> TMEM cols 256 h
+            const uint64_t ad = sm100::umma_desc_sw128(a0 + h * 128 * 128 + kk * 32, 16, A_SBO);
+            sm100::umma_f16(tmem_d + 256 * h, ad, bd, kIdesc, (kt | kk) != 0);
+          }
         }
         sm100::umma_commit(bar_tempty(ts));      // x tile and packed inputs consumed
         sm100::umma_commit(bar_bempty(bs));      // dequantized B consumed
@@ -215,11 +231,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     sm100::tc_fence_after();
     if (ok && !*abort_flag) {
       const int q = warp & 3;                  // TMEM lane quarter this warp may access
-      const int chalf = dw >> 2;               // columns [128 chalf, 128 chalf + 128)
-      const int row = tile_m * BM + q * 32 + lane;
-      const uint32_t taddr = tmem_d + ((uint32_t)(q * 32) << 16);
+      const int half = dw >> 2;                // the two warps of a quarter split the work
+      // NACC == 1: split the 256 columns; NACC == 2: one accumulator (128 rows) each
+      const int acc = NACC == 2 ? half : 0;
+      const int c_lo = NACC == 2 ? 0 : half * 4, c_hi = NACC == 2 ? 8 : half * 4 + 4;
+      const int row = tile_m * BM + acc * 128 + q * 32 + lane;
+      const uint32_t taddr = tmem_d + acc * 256 + ((uint32_t)(q * 32) << 16);
 #pragma unroll 1
-      for (int c = chalf * 4; c < chalf * 4 + 4; ++c) {
+      for (int c = c_lo; c < c_hi; ++c) {
         uint32_t v[32];
         sm100::tmem_ld_32x32b_x32(taddr + c * 32, v);
         sm100::tmem_ld_wait();
@@ -315,6 +334,8 @@ cudaError_t launch_gemm_tc(const void* x, int64_t ldx, const int32_t* qweight,
     *why = "out must be 16-byte aligned with ldo % 8 == 0";
     return cudaSuccess;
   }
+  const int nacc = M > 128 ? 2 : 1;
+  const int BM = 128 * nacc;
   CUtensorMap tmA, tmW, tmS, tmZ;
   const int G = K / group_size;
   bool ok = make_map_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, K, M, (uint64_t)ldx * 2, BK, BM,
@@ -332,8 +353,12 @@ cudaError_t launch_gemm_tc(const void* x, int64_t ldx, const int32_t* qweight,
   static std::once_flag attr_once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(attr_once, [] {
-    attr_err = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)SMEM_BYTES);
+    attr_err = cudaFuncSetAttribute(gemm_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)Geo<1>::SMEM_BYTES);
+    if (attr_err == cudaSuccess)
+      attr_err = cudaFuncSetAttribute(gemm_tc_kernel<2>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)Geo<2>::SMEM_BYTES);
   });
   if (attr_err != cudaSuccess) return attr_err;
   TcArgs a;
@@ -342,7 +367,10 @@ cudaError_t launch_gemm_tc(const void* x, int64_t ldx, const int32_t* qweight,
   a.M = M; a.N = N; a.K = K; a.gs = group_size;
   a.status = dev_status;
   dim3 grid((M + BM - 1) / BM, (N + BN - 1) / BN);
-  gemm_tc_kernel<<<grid, kThreads, SMEM_BYTES, stream>>>(tmA, tmW, tmS, tmZ, a);
+  if (nacc == 2)
+    gemm_tc_kernel<2><<<grid, kThreads, Geo<2>::SMEM_BYTES, stream>>>(tmA, tmW, tmS, tmZ, a);
+  else
+    gemm_tc_kernel<1><<<grid, kThreads, Geo<1>::SMEM_BYTES, stream>>>(tmA, tmW, tmS, tmZ, a);
   return cudaGetLastError();
 }
 

@@ -100,12 +100,36 @@ __device__ __forceinline__ float ld_dsmem_f32(uint32_t local_addr, uint32_t rank
 // Biased unpack: 4 half2 holding (1024 + w) for nibbles at bits 0..3 / 16..19 and
 // (1024 + 16 w) for bits 4..7 / 20..23, of the word and of word >> 8 -- exact values,
 // element pairs (0,1), (2,3), (4,5), (6,7).  No zero subtraction per weight.
-__device__ __forceinline__ void unpack_biased(uint32_t w, uint32_t d[4]) {
+// `magic` (0x64006400) arrives in a register whose value the compiler cannot see, so
+// each lop3 keeps one immediate (the mask) and one register operand and stays a single
+// instruction.
+__device__ __forceinline__ void unpack_biased(uint32_t w, uint32_t magic, uint32_t d[4]) {
+#if AWQ_DEC_OPAQUE == 0
   const uint32_t w8 = w >> 8;
   d[0] = lop3_and_or(w, kLoMask, kMagic);
   d[1] = lop3_and_or(w, kHiMask, kMagic);
   d[2] = lop3_and_or(w8, kLoMask, kMagic);
   d[3] = lop3_and_or(w8, kHiMask, kMagic);
+#elif AWQ_DEC_OPAQUE == 1
+  const uint32_t w8 = w >> 8;
+  d[0] = lop3_and_or(w, kLoMask, magic);
+  d[1] = lop3_and_or(w, kHiMask, magic);
+  d[2] = lop3_and_or(w8, kLoMask, magic);
+  d[3] = lop3_and_or(w8, kHiMask, magic);
+#else
+  const uint32_t w8 = w >> 8;
+  const uint32_t lo = magic >> 16, hi = lo << 4;   // opaque masks too: 0x6400 -> not used
+  d[0] = lop3_and_or(w, kLoMask, magic);
+  d[1] = lop3_and_or(w, kHiMask, magic);
+  d[2] = lop3_and_or(w8, kLoMask, magic);
+  d[3] = lop3_and_or(w8, kHiMask, magic);
+  (void)lo; (void)hi;
+#endif
+}
+__device__ __forceinline__ uint32_t opaque_u32(uint32_t v) {
+  uint32_t r;
+  asm volatile("mov.b32 %0, %1;" : "=r"(r) : "r"(v));
+  return r;
 }
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   uint32_t r;
@@ -113,8 +137,21 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   return r;
 }
 
+// Tuning knobs (compile time): CTAs per SM the M<=4 variant is built for (register
+// budget 65536 / (256 * AWQ_DEC_MINB)), and how many stages each warp prefetches into L2
+// before the grid dependency wait.
+#ifndef AWQ_DEC_MINB
+#define AWQ_DEC_MINB 2
+#endif
+#ifndef AWQ_DEC_L2PF
+#define AWQ_DEC_L2PF 0
+#endif
+#ifndef AWQ_DEC_OPAQUE
+#define AWQ_DEC_OPAQUE 1
+#endif
+
 template <int TOKSETS>
-__global__ void __launch_bounds__(kThreads, TOKSETS == 1 ? 2 : 1)
+__global__ void __launch_bounds__(kThreads, TOKSETS == 1 ? AWQ_DEC_MINB : 1)
 gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
   constexpr int MP = 4 * TOKSETS;
   // BIAS (one 4-token set): the MMAs accumulate x * (1024 + w) / x * (1024 + 16 w)
@@ -168,7 +205,7 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
     for (int s = 0; s < kStages; ++s) sm100::mbar_init(bars + 8 * s, 1);
     sm100::fence_mbar_init();
     sm100::prefetch_tmap(&tmW);
-    for (int j = 0; j < 2 * kStages && j < nst; ++j)
+    for (int j = 0; j < AWQ_DEC_L2PF && j < nst; ++j)
       sm100::tma_prefetch_l2_2d(&tmW, strip * 32, (b0 + 2 * j) * 8);
   }
   sm100::grid_dependency_wait();
@@ -211,6 +248,7 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
   __syncthreads();
   const int grp0 = krow0 / a.gs;                      // first group staged in zs / ss
 
+  const uint32_t magic = opaque_u32(kMagic);
   const int chunk = (g >> 1) | ((g & 1) << 2);       // conflict-free word chunk
   // B column g = (token g/2, pair slot g%2): x goes to the low half for slot 0 and
   // to the high half for slot 1 (prmt selector; bytes 4..7 come from the zero word)
@@ -333,8 +371,8 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
         for (int c = 0; c < 4; ++c) {
           uint32_t da[4], db[4];
           if constexpr (BIAS) {
-            unpack_biased(wa[c], da);
-            unpack_biased(wb[c], db);
+            unpack_biased(wa[c], magic, da);
+            unpack_biased(wb[c], magic, db);
           } else {
             dequant_word(wa[c], zcst[c], scl[c], da);
             dequant_word(wb[c], zcst[c], scl[c], db);
@@ -435,12 +473,13 @@ size_t smem_bytes(int xs_stride, int ngrp) {
          (size_t)MP * xs_stride * 2 + (size_t)ngrp * (128 + kStripN * 2);
 }
 
-// Programmatic dependent launch is on unless AWQ_PDL=0 (read once per process).
+// Programmatic dependent launch is off unless AWQ_PDL=1 (read once per process): on the
+// mixed decode stack it measured slower than plain stream order.
 bool pdl_enabled() {
   static int v = -1;
   if (v < 0) {
     const char* e = getenv("AWQ_PDL");
-    v = (e && e[0] == '0') ? 0 : 1;
+    v = (e && e[0] == '1') ? 1 : 0;
   }
   return v == 1;
 }

@@ -1,0 +1,97 @@
+"""GPU: tensor-parallel AWQ linears over NCCL (one process per GPU), checked against the
+single-GPU product.  Needs >= 2 GPUs; skipped otherwise.
+
+Bar: max |tp - single| / max |single| <= 1e-2 (the parity tolerance used everywhere).
+"""
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-2
+HIDDEN, INTER = 3584, 18944
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _layers(seed):
+    gu = O.make_awq_layer(HIDDEN, 2 * INTER, 128, seed=seed)
+    dn = O.make_awq_layer(INTER, HIDDEN, 128, seed=seed + 1)
+    o = O.make_awq_layer(HIDDEN, HIDDEN, 128, seed=seed + 2)
+    return gu, dn, o
+
+
+def _worker(rank, world, port, M, seed, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    import datetime
+    import sys
+    sys.path.insert(0, os.environ["AWQ_PKG"])
+    sys.path.insert(0, os.environ["AWQ_REPO"])
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60), device_id=dev)
+    try:
+        from awq_b200 import tp
+        gu, dn, o = _layers(seed)
+        to = lambda t: tuple(torch.from_numpy(np.ascontiguousarray(a)).to(dev) for a in t)
+        x = torch.from_numpy(O.make_x(M, HIDDEN, seed=seed + 3)).to(dev)
+        mlp = tp.TensorParallelMLP(tp.AWQWeights(*to(gu)), tp.AWQWeights(*to(dn)), INTER, world, rank)
+        y = mlp(x)
+        ro = tp.RowParallelAWQ(tp.AWQWeights(*to(o)), world, rank)
+        z = ro(x[:, ro.k0:ro.k1].contiguous())
+        torch.cuda.synchronize()
+        q.put((rank, y.float().cpu().numpy(), z.float().cpu().numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("M", [1, 512])
+def test_tp_world2_matches_single_gpu(cuda, M):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import awq_b200
+    from conftest import PKG, REPO
+    world, seed = 2, 21
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    env = dict(os.environ, AWQ_PKG=str(PKG), AWQ_REPO=str(REPO))
+    os.environ.update(env)
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, M, seed, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        rank, y, z = q.get(timeout=300)
+        res[rank] = (y, z)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    # single-GPU reference through the same library
+    gu, dn, o = _layers(seed)
+    to = lambda t: tuple(torch.from_numpy(np.ascontiguousarray(a)).to(cuda) for a in t)
+    x = torch.from_numpy(O.make_x(M, HIDDEN, seed=seed + 3)).to(cuda)
+    g = awq_b200.gemm(x, *to(gu), 128)
+    h = (torch.nn.functional.silu(g[:, :INTER].float()) * g[:, INTER:].float()).half()
+    y_ref = awq_b200.gemm(h, *to(dn), 128).float().cpu().numpy()
+    z_ref = awq_b200.gemm(x, *to(o), 128).float().cpu().numpy()
+    for rank in range(world):
+        y, z = res[rank]
+        assert O.max_rel_err(y, y_ref) <= TOL, rank
+        assert O.max_rel_err(z, z_ref) <= TOL, rank
