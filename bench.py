@@ -405,28 +405,55 @@ def decode_sweep(torch, lib, awq_b200, dev, hbm_peak):
 
 # ------------------------------------------------------------------ reference arm ----
 def run_reference(args):
-    """The reference's own CPU implementation of the path (dequantize, then fp32
-    matmul on the host), on this arm's metric and config, rank 0 only."""
+    """The reference's own CPU implementation of the path (dequantize, then fp32 matmul on
+    the host cores), on this arm's metric: W untimed and K timed steps, each step a bounded
+    sample of the workload -- one Qwen2-7B layer's 4 linears at M=1 (1/28 of a decode
+    token).  Rank 0 only; other ranks exit without work."""
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
     import torch
-    cb = cpu_baseline(torch, sample_seconds=max(2.0, args.cpu_seconds / max(1, args.steps)))
-    value = cb["value"]
-    per_layer = sum(alg_bytes(1, K, N) for (_, K, N) in STACK)
-    ms = per_layer * LAYERS / (value * 1e12) * 1e3
+    from oracle import oracle as O
+    threads = O.cpu_threads()
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(11)
+    layers = []
+    for _, K, N in STACK:
+        qw = torch.randint(-2**31, 2**31, (K, N // 8), dtype=torch.int64, generator=g).to(torch.int32)
+        qz = torch.randint(-2**31, 2**31, (K // GS, N // 8), dtype=torch.int64, generator=g).to(torch.int32)
+        s = (torch.rand((K // GS, N), generator=g) * 0.018 + 0.002).half()
+        x = torch.randn((1, K), generator=g).half()
+        layers.append((x, qw, qz, s))
+    step_bytes = sum(alg_bytes(1, K, N) for (_, K, N) in STACK)
+
+    def step():
+        for (x, qw, qz, s) in layers:
+            O.torch_awq_gemm_f32(x, qw, qz, s)
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    secs = time.perf_counter() - t0
+    value = step_bytes * args.steps / secs / 1e12
+    sample = (f"{args.steps} steps of one Qwen2-7B layer (qkv, o, gate_up, down) at M=1: torch "
+              f"dequant + fp32 matmul on {threads} host threads, {secs:.1f} s")
     print(json.dumps({
         "impl": "reference",
         "metric": "AWQ GEMM HBM TB/s (M=1 decode) & TFLOPS (M=2048 prefill), % of B200 roofline",
         "value": round(value, 6), "unit": "TB/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "warmup": args.warmup, "ms_per_step": round(secs * 1e3 / args.steps, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded random int4 AWQ weights, x ~ N(0,1); no checkpoint)",
         "config": {"workload": "decode M=1 through the AWQ linears of the 28-layer Qwen2-7B "
-                               "stack (timed on a bounded sample: one layer's 4 linears)",
+                               "stack (qkv 3584x4608, o 3584x3584, gate_up 3584x37888, down "
+                               "18944x3584 per layer); each timed step is one layer's 4 linears",
                    "path": "reference dequantize-then-matmul on host cores (oracle port of "
-                           "test/compare_benchmark.py:72-95 with an fp32 matmul)"},
-        "cpu_baseline": cb,
+                           "test/compare_benchmark.py:72-95 with an fp32 matmul)",
+                   "group_size": GS},
+        "cpu_baseline": {"value": round(value, 6), "unit": "TB/s", "cores": threads,
+                         "kind": "port", "sample": sample},
         "e2e": {"value": round(value, 6), "unit": "TB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }))

@@ -6,15 +6,14 @@
 // (songqiuyu/Qwen2-7B-Triton_Engine kernels/awq_gemm.py:251-266) and small-M calls
 // of _awq_gemm_kernel (kernels/awq_gemm.py:152-228).
 //
-// Roles (one CTA = 8 consumer warps + 1 producer warp, one CTA per SM)
-//   producer  lane 0 of warp 8 keeps every consumer's ring full: per stage it waits for
-//             the stage's "empty" mbarrier, then issues one 2-D TMA load of 32 K-rows x
-//             32 packed words (4 KB, 128-byte swizzle) completing on the "full" mbarrier.
-//   consumer  warp w owns a contiguous, stage-aligned range of the CTA's K rows.  It walks
-//             it one quantization group at a time; the inner loop over the group's
-//             stages is branch-free apart from the full-barrier wait: 8 x (2 shared loads
-//             + biased unpack + 8 mma.sync) per stage, then one arrive on "empty".  The
-//             group's zero/scale correction runs once per group, outside that loop.
+// Roles (one CTA = 8 warps, one CTA per SM)
+//   every warp owns a contiguous, stage-aligned range of the CTA's K rows and a ring of
+//   shared-memory stages it refills itself: one 2-D TMA load of 32 K-rows x 32 packed
+//   words (4 KB, 128-byte swizzle) per stage, completing on the stage's mbarrier.  It
+//   walks its range one quantization group at a time; the inner loop over the group's
+//   stages is branch-free apart from the barrier wait and the refill: 4 x (2 shared
+//   loads + biased unpack + 8 mma.sync) per stage.  The group's zero/scale correction
+//   runs once per group, outside that loop.
 //   lane (g = lane/4, t = lane%4) reads rows t and t+4 of each 8-row block as 16 bytes
 //   from word chunk c(g) = (g >> 1) | ((g & 1) << 2); with the swizzle (chunk ^ row)
 //   the 8 lanes of each shared-memory phase hit 8 distinct 16-byte bank groups.
@@ -25,9 +24,10 @@
 //   fp32 scale (scale / 16) is applied; for M > 4 W is rounded to fp16 first exactly as
 //   the reference does.
 // Split-K: the CS CTAs of a thread-block cluster split K for one 256-column strip; each
-//   reduces its 8 warps in shared memory, then after a cluster barrier CTA r sums column
-//   slice r of all CS partials through distributed shared memory (fixed rank order, so
-//   the result is deterministic) and writes fp16.  No global workspace, no atomics.
+//   sums its 8 warps' partials in shared memory (one barrier, fixed order), then after a
+//   cluster barrier CTA r sums column slice r of all CS partials through distributed
+//   shared memory (fixed rank order, so the result is deterministic) and writes fp16.
+//   With CS = 1 the CTA writes its sum directly.  No global workspace, no atomics.
 // Every mbarrier wait is bounded (status word + early exit); both cluster barriers are
 // reached by every thread on every path, so a time-out never strands a peer CTA.
 #include <cuda.h>
@@ -44,8 +44,8 @@ namespace awq {
 
 namespace {
 
-constexpr int kConsumers = 8;                     // compute warps
-constexpr int kThreads = (kConsumers + 1) * 32;   // + one TMA producer warp
+constexpr int kConsumers = 8;                     // warps per CTA
+constexpr int kThreads = kConsumers * 32;
 constexpr int kRowsPerStage = 32;                 // four 8-row blocks per TMA copy
 constexpr int kBlocksPerStage = kRowsPerStage / 8;
 constexpr int kStripN = 256;
@@ -54,8 +54,12 @@ constexpr int kRedStride = 264;
 
 template <int TOKSETS>
 struct DecGeo {
-  static constexpr int kStages = TOKSETS == 1 ? 4 : 2;              // per-consumer ring depth
+  static constexpr int kStages = TOKSETS == 1 ? 4 : 2;              // per-warp ring depth
   static constexpr uint32_t kRingBytes = kConsumers * kStages * kStageBytes;
+  // row stride (floats) of a warp's partial sums parked in its own ring after the loop;
+  // MP rows of it must fit the warp's kStages * 4 KB
+  static constexpr int kPartStride = TOKSETS == 1 ? kRedStride : kStripN;
+  static_assert(4 * TOKSETS * kPartStride * 4 <= kStages * (int)kStageBytes, "partials fit the ring");
 };
 
 struct TmaGemvArgs {
@@ -86,6 +90,12 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   uint4 v;
   asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+
+__device__ __forceinline__ uint32_t lds_u16(uint32_t addr) {
+  uint16_t v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
   return v;
 }
 
@@ -141,11 +151,10 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
   const uint32_t base_raw = sm100::smem_u32(smem_raw);
   const uint32_t sbase = (base_raw + 1023u) & ~1023u;
   unsigned char* sgen = smem_raw + (sbase - base_raw);
-  // layout: ring | red (MP x 264 fp32) | full bars | empty bars | abort | xs | zs | ss
+  // layout: ring | red (MP x 264 fp32) | stage bars | abort | xs | zs | ss
   const uint32_t off_red = DecGeo<TOKSETS>::kRingBytes;
   const uint32_t off_full = off_red + MP * kRedStride * 4;
-  const uint32_t off_empty = off_full + kConsumers * kStages * 8;
-  const uint32_t off_misc = off_empty + kConsumers * kStages * 8;
+  const uint32_t off_misc = off_full + kConsumers * kStages * 8;
   const uint32_t off_xs = off_misc + 16;
   const uint32_t off_zs = off_xs + (uint32_t)MP * a.xs_stride * 2;
   const uint32_t off_ss = off_zs + (uint32_t)a.ngrp_cta * 128;
@@ -169,35 +178,30 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
   const int krow0 = cb0 * 8;
   const int Kc = nb * 8;
   auto full_bar = [&](int w, int s) { return sbase + off_full + (uint32_t)(w * kStages + s) * 8u; };
-  auto empty_bar = [&](int w, int s) { return sbase + off_empty + (uint32_t)(w * kStages + s) * 8u; };
   auto stage_addr = [&](int w, int s) {
     return sbase + (uint32_t)(w * kStages + s) * kStageBytes;
   };
 
-  if (tid == 0) {
-    for (int i = 0; i < kConsumers * kStages; ++i) {
-      sm100::mbar_init(sbase + off_full + 8u * i, 1);
-      sm100::mbar_init(sbase + off_empty + 8u * i, 1);
-    }
+  // every warp initialises its own stage barriers and starts its own stream
+  int b0, b1;
+  warp_range(cb0, nb, warp, b0, b1);
+  const int nst = (b1 - b0) / kBlocksPerStage;
+  if (lane == 0) {
+    for (int s2 = 0; s2 < kStages; ++s2) sm100::mbar_init(full_bar(warp, s2), 1);
     sm100::fence_mbar_init();
-    *abort_flag = 0;
-    sm100::prefetch_tmap(&tmW);
+    if (warp == 0) {
+      *abort_flag = 0;
+      sm100::prefetch_tmap(&tmW);
+    }
   }
   sm100::grid_dependency_wait();        // no-op unless launched as a programmatic dependent
   sm100::grid_launch_dependents();
-  __syncthreads();
-
-  // ---- producer: the first kStages stages of every consumer, before the staging -----
-  if (warp == kConsumers && lane == 0) {
-    for (int w = 0; w < kConsumers; ++w) {
-      int wb0, wb1;
-      warp_range(cb0, nb, w, wb0, wb1);
-      const int nst = (wb1 - wb0) / kBlocksPerStage;
-      for (int j = 0; j < kStages && j < nst; ++j) {
-        sm100::mbar_arrive_expect_tx(full_bar(w, j), kStageBytes);
-        sm100::tma_load_2d(stage_addr(w, j), &tmW, full_bar(w, j), strip * 32,
-                           (wb0 + j * kBlocksPerStage) * 8);
-      }
+  __syncwarp();
+  if (lane == 0) {
+    for (int j = 0; j < kStages && j < nst; ++j) {
+      sm100::mbar_arrive_expect_tx(full_bar(warp, j), kStageBytes);
+      sm100::tma_load_2d(stage_addr(warp, j), &tmW, full_bar(warp, j), strip * 32,
+                         (b0 + j * kBlocksPerStage) * 8);
     }
   }
 
@@ -239,53 +243,16 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[s2][q][i] = 0.f;
 
-  if (warp == kConsumers) {
-    // ---- producer: refill every ring as its consumer frees stages -----------------
-    if (lane == 0) {
-      // warp ranges are equal-sized except at the end of the CTA range, so consumer 0
-      // has the most stages
-      int b0_, b1_;
-      warp_range(cb0, nb, 0, b0_, b1_);
-      const int maxst = (b1_ - b0_) / kBlocksPerStage;
-      int j_stop = maxst;                               // first stage not issued everywhere
-      for (int j = kStages; j < maxst && j_stop == maxst; ++j) {
-        const int s = j % kStages;
-        for (int w = 0; w < kConsumers; ++w) {
-          warp_range(cb0, nb, w, b0_, b1_);
-          if (j >= (b1_ - b0_) / kBlocksPerStage) continue;
-          if (*abort_flag ||
-              !sm100::mbar_wait_bounded(empty_bar(w, s), ((j / kStages) - 1) & 1, a.status)) {
-            *abort_flag = 1;
-            j_stop = j;
-            break;
-          }
-          sm100::mbar_arrive_expect_tx(full_bar(w, s), kStageBytes);
-          sm100::tma_load_2d(stage_addr(w, s), &tmW, full_bar(w, s), strip * 32,
-                             (b0_ + j * kBlocksPerStage) * 8);
-        }
-      }
-      if (j_stop < maxst) {
-        // a consumer stopped: wait (bounded) until every copy issued so far has landed
-        for (int w = 0; w < kConsumers; ++w) {
-          warp_range(cb0, nb, w, b0_, b1_);
-          const int last = min(j_stop + 1, (b1_ - b0_) / kBlocksPerStage);
-          for (int j = max(0, last - kStages); j < last; ++j)
-            sm100::mbar_wait_bounded(full_bar(w, j % kStages), (j / kStages) & 1, nullptr,
-                                     50000000ull);
-        }
-      }
-    }
-    __syncwarp();
-  } else {
-    // ---- consumer warp -----------------------------------------------------------
-    int b0, b1;
-    warp_range(cb0, nb, warp, b0, b1);
+  {
     const uint32_t bsel = (g & 1) ? 0x1054u : 0x5410u;   // x into this lane's pair slot
     const uint32_t lane_off_a = (uint32_t)t * 128u + ((uint32_t)(chunk ^ t) << 4);
     const uint32_t lane_off_b = (uint32_t)(t + 4) * 128u + ((uint32_t)(chunk ^ (t + 4)) << 4);
-    const __half* xrow[TOKSETS];
+    // shared-memory byte address of x[token][k = 0] for this lane's tokens (k is added
+    // per block); explicit ld.shared keeps these loads off the L1TEX path
+    uint32_t xrow[TOKSETS];
 #pragma unroll
-    for (int s2 = 0; s2 < TOKSETS; ++s2) xrow[s2] = xs + (4 * s2 + (g >> 1)) * a.xs_stride + t - krow0;
+    for (int s2 = 0; s2 < TOKSETS; ++s2)
+      xrow[s2] = sbase + off_xs + (uint32_t)(((4 * s2 + (g >> 1)) * a.xs_stride + t - krow0) * 2);
     uint32_t zcst[4][4], scl[4][4];
     float pacc[BIAS ? 8 : 1][4];
     int j = 0;                                          // stage counter of this warp
@@ -296,12 +263,12 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
       const int gl = grp - grp0;
       if constexpr (!BIAS) {
         // fp16 W path: zeros and scales are used per weight
-        const uint4 z4 = reinterpret_cast<const uint4*>(zs + gl * 32)[chunk];
+        const uint4 z4 = lds128(sbase + off_zs + (uint32_t)(gl * 128 + chunk * 16));
         const uint32_t zw[4] = {z4.x, z4.y, z4.z, z4.w};
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           zero_consts(zw[c], zcst[c]);
-          const uint4 s4 = reinterpret_cast<const uint4*>(ss + gl * kStripN)[chunk * 4 + c];
+          const uint4 s4 = lds128(sbase + off_ss + (uint32_t)(gl * kStripN * 2 + (chunk * 4 + c) * 16));
           scl[c][0] = s4.x; scl[c][1] = s4.y; scl[c][2] = s4.z; scl[c][3] = s4.w;
         }
       } else {
@@ -327,9 +294,9 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
           uint32_t bf0[TOKSETS], bf1[TOKSETS];
 #pragma unroll
           for (int s2 = 0; s2 < TOKSETS; ++s2) {
-            const __half* xp = xrow[s2] + krow + h * 8;
-            bf0[s2] = prmt(__half_as_ushort(xp[0]), 0u, bsel);
-            bf1[s2] = prmt(__half_as_ushort(xp[4]), 0u, bsel);
+            const uint32_t xa = xrow[s2] + (uint32_t)(krow + h * 8) * 2u;
+            bf0[s2] = prmt(lds_u16(xa), 0u, bsel);
+            bf1[s2] = prmt(lds_u16(xa + 8u), 0u, bsel);
           }
           const uint32_t wa[4] = {va.x, va.y, va.z, va.w};
           const uint32_t wb[4] = {vb.x, vb.y, vb.z, vb.w};
@@ -358,16 +325,22 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
             }
           }
         }
-        // every lane's loads from this stage were consumed by the MMAs above
+        // refill this stage with stage j + kStages: every lane's loads from it were
+        // consumed by the MMAs above
         __syncwarp();
-        if (lane == 0) sm100::mbar_arrive(empty_bar(warp, s));
+        if (lane == 0 && j + kStages < nst) {
+          sm100::mbar_arrive_expect_tx(full_bar(warp, s), kStageBytes);
+          sm100::tma_load_2d(st, &tmW, full_bar(warp, s), strip * 32,
+                             (b0 + (j + kStages) * kBlocksPerStage) * 8);
+        }
       }
       if constexpr (BIAS) {
         // close the group segment [kb, kend): remove the zero term, apply the scale
         float part = 0.f;
         const int u0 = (kb - krow0) >> 3, u1 = (kend - krow0) >> 3;
+        const uint32_t xt = sbase + off_xs + (uint32_t)(t * a.xs_stride) * 2u;
         for (int u = u0 + g; u < u1; u += 8) {
-          const uint4 v = *reinterpret_cast<const uint4*>(xs + t * a.xs_stride + u * 8);
+          const uint4 v = lds128(xt + (uint32_t)u * 16u);
           const uint32_t hv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
@@ -378,11 +351,11 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
         part += __shfl_xor_sync(0xffffffffu, part, 4);
         part += __shfl_xor_sync(0xffffffffu, part, 8);
         part += __shfl_xor_sync(0xffffffffu, part, 16);   // sum(x[token t]) over the segment
-        const uint4 z4 = reinterpret_cast<const uint4*>(zs + gl * 32)[chunk];
+        const uint4 z4 = lds128(sbase + off_zs + (uint32_t)(gl * 128 + chunk * 16));
         const uint32_t zw[4] = {z4.x, z4.y, z4.z, z4.w};
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          const uint4 s4 = reinterpret_cast<const uint4*>(ss + gl * kStripN)[chunk * 4 + c];
+          const uint4 s4 = lds128(sbase + off_ss + (uint32_t)(gl * kStripN * 2 + (chunk * 4 + c) * 16));
           const uint32_t sv[4] = {s4.x, s4.y, s4.z, s4.w};
           const uint32_t z8 = zw[c] >> 8;
           const uint32_t zb[4] = {lop3_and_or(zw[c], kLoMask, kMagic),   // 1024 + z
@@ -405,34 +378,49 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
       }
       kb = kend;
     }
+    if (!ok && lane == 0) {
+      // a stage never arrived: wait (bounded) for this warp's copies still in flight
+      for (int jj = j; jj < nst && jj < j + kStages; ++jj)
+        sm100::mbar_wait_bounded(full_bar(warp, jj % kStages), (jj / kStages) & 1, nullptr,
+                                 50000000ull);
+    }
+    __syncwarp();
   }
 
-  // ---- CTA reduction: consumer warps add into red[m][n] in fixed order -------------
-  for (int w = 0; w < kConsumers; ++w) {
-    if (warp == w) {
+  // ---- CTA reduction: each warp parks its partial in its own (now idle) ring, one
+  // barrier, then the 8 partials are summed in warp order -------------------------------
+  {
+    float* mine = reinterpret_cast<float*>(sgen + (uint32_t)warp * kStages * kStageBytes);
 #pragma unroll
-      for (int s2 = 0; s2 < TOKSETS; ++s2) {
-        const int m = 4 * s2 + t;
+    for (int s2 = 0; s2 < TOKSETS; ++s2) {
+      const int m = 4 * s2 + t;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          float4* dst = reinterpret_cast<float4*>(red + m * kRedStride + 32 * chunk + 4 * q);
-          if (w == 0) {
-            *dst = make_float4(acc[s2][q][0], acc[s2][q][1], acc[s2][q][2], acc[s2][q][3]);
-          } else {
-            float4 v = *dst;
-            v.x += acc[s2][q][0]; v.y += acc[s2][q][1]; v.z += acc[s2][q][2]; v.w += acc[s2][q][3];
-            *dst = v;
-          }
-        }
-      }
+      for (int q = 0; q < 8; ++q)
+        *reinterpret_cast<float4*>(mine + m * DecGeo<TOKSETS>::kPartStride + 32 * chunk + 4 * q) =
+            make_float4(acc[s2][q][0], acc[s2][q][1], acc[s2][q][2], acc[s2][q][3]);
     }
-    __syncthreads();
   }
+  __syncthreads();
+  const int nbase = strip * kStripN;
+  for (int idx = tid; idx < MP * kStripN; idx += kThreads) {
+    const int m = idx / kStripN, nl = idx - m * kStripN;
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < kConsumers; ++w)
+      v += reinterpret_cast<const float*>(sgen + (uint32_t)w * kStages * kStageBytes)
+               [m * DecGeo<TOKSETS>::kPartStride + nl];
+    if (a.cs == 1) {
+      const int n = nbase + nl;
+      if (m < Mc && n < a.N) a.out[(int64_t)(m0 + m) * a.ldo + n] = __float2half_rn(v);
+    } else {
+      red[m * kRedStride + nl] = v;
+    }
+  }
+  if (a.cs == 1) return;                               // grid-uniform: no cluster to serve
 
   // ---- cluster reduction over distributed shared memory ----------------------------
   cluster_sync_all();                                  // every CTA's red is complete
   const int cw = kStripN / a.cs;                       // columns reduced by this CTA
-  const int nbase = strip * kStripN;
   const uint32_t red_addr = sbase + off_red;
   for (int idx = tid; idx < Mc * cw; idx += kThreads) {
     const int m = idx / cw;
@@ -474,7 +462,7 @@ size_t smem_bytes(int xs_stride, int ngrp) {
   const int MP = 4 * TOKSETS;
   constexpr int S = DecGeo<TOKSETS>::kStages;
   return 1024 + DecGeo<TOKSETS>::kRingBytes + (size_t)MP * kRedStride * 4 +
-         2 * kConsumers * S * 8 + 16 + (size_t)MP * xs_stride * 2 + (size_t)ngrp * (128 + kStripN * 2);
+         kConsumers * S * 8 + 16 + (size_t)MP * xs_stride * 2 + (size_t)ngrp * (128 + kStripN * 2);
 }
 
 // Cluster size: grow the split-K factor while the grid stays within one CTA per SM and
