@@ -74,6 +74,7 @@ struct TmaGemvArgs {
   int bps;         // 8-row blocks per CTA (multiple of kBlocksPerStage)
   int xs_stride;   // halves per token row of xs
   int ngrp_cta;    // quantization groups a CTA's K range can touch (zs / ss rows)
+  int l2pf;        // weight stages each warp prefetches into L2 before the dependency wait
   int* status;
 };
 
@@ -97,6 +98,18 @@ __device__ __forceinline__ uint32_t lds_u16(uint32_t addr) {
   uint16_t v;
   asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
   return v;
+}
+
+// 16-byte asynchronous global -> shared copy (no register round trip); completion is
+// awaited with cp_async_wait_all.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+__device__ __forceinline__ void sts128_zero(uint32_t dst) {
+  asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(dst), "r"(0u) : "memory");
 }
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -193,6 +206,12 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
       *abort_flag = 0;
       sm100::prefetch_tmap(&tmW);
     }
+    // Under programmatic dependent launch this part overlaps the previous kernel: an L2
+    // prefetch of the first weight stages is safe before the dependency is resolved
+    // (L2 stays coherent with the previous kernel's writes); the copies into shared
+    // memory are issued only after griddepcontrol.wait.
+    for (int j = 0; j < a.l2pf && j < nst; ++j)
+      sm100::tma_prefetch_l2_2d(&tmW, strip * 32, (b0 + j * kBlocksPerStage) * 8);
   }
   sm100::grid_dependency_wait();        // no-op unless launched as a programmatic dependent
   sm100::grid_launch_dependents();
@@ -206,30 +225,35 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
   }
 
   // ---- stage activations xs[m][k] and the strip's zeros / scales ---------------------
+  // asynchronous 16-byte copies: every thread's copies are in flight at once, so the
+  // staging costs one memory round trip (it overlaps the first weight stages)
   {
     const int vecs = Kc / 8;                         // 16-byte vectors per token row
     for (int i = tid; i < MP * vecs; i += kThreads) {
       const int m = i / vecs, v = i - m * vecs;
-      uint4 val = make_uint4(0, 0, 0, 0);
+      const uint32_t dst = sbase + off_xs + (uint32_t)(m * a.xs_stride + v * 8) * 2u;
       if (m < Mc)
-        val = __ldg(reinterpret_cast<const uint4*>(a.x + (int64_t)(m0 + m) * a.ldx + krow0) + v);
-      *reinterpret_cast<uint4*>(xs + m * a.xs_stride + v * 8) = val;
+        cp_async16(dst, a.x + (int64_t)(m0 + m) * a.ldx + krow0 + v * 8);
+      else
+        sts128_zero(dst);
     }
     const int g0 = krow0 / a.gs;
     const int ng = Kc > 0 ? (krow0 + Kc - 1) / a.gs - g0 + 1 : 0;
     for (int i = tid; i < ng * 40; i += kThreads) {
       const int gi = i / 40, v = i - gi * 40;      // 8 vectors of zeros, 32 of scales
-      uint4 val = make_uint4(0, 0, 0, 0);
       if (v < 8) {
         const int wc = strip * 32 + v * 4;
-        if (wc < a.PN) val = __ldg(reinterpret_cast<const uint4*>(a.qz + (int64_t)(g0 + gi) * a.PN + wc));
-        reinterpret_cast<uint4*>(zs + gi * 32)[v] = val;
+        const uint32_t dst = sbase + off_zs + (uint32_t)(gi * 128 + v * 16);
+        if (wc < a.PN) cp_async16(dst, a.qz + (int64_t)(g0 + gi) * a.PN + wc);
+        else sts128_zero(dst);
       } else {
         const int n = strip * kStripN + (v - 8) * 8;
-        if (n < a.N) val = __ldg(reinterpret_cast<const uint4*>(a.scales + (int64_t)(g0 + gi) * a.N + n));
-        reinterpret_cast<uint4*>(ss + gi * kStripN)[v - 8] = val;
+        const uint32_t dst = sbase + off_ss + (uint32_t)(gi * kStripN * 2 + (v - 8) * 16);
+        if (n < a.N) cp_async16(dst, a.scales + (int64_t)(g0 + gi) * a.N + n);
+        else sts128_zero(dst);
       }
     }
+    cp_async_wait_all();
   }
   __syncthreads();
   const int grp0 = krow0 / a.gs;
@@ -585,6 +609,7 @@ cudaError_t launch_gemv_tma(const void* x, int64_t ldx, const int32_t* qweight,
   a.bps = p.bps;
   a.xs_stride = p.xs_stride;
   a.ngrp_cta = p.ngrp;
+  a.l2pf = pdl_enabled() ? 4 : 0;
   a.status = dev_status;
   const int64_t chunk = 4 * p.toksets;                 // tokens per CTA row of the grid
   const int64_t max_rows = (int64_t)65535 * chunk;
