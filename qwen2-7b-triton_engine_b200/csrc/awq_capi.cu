@@ -42,7 +42,6 @@ __device__ int g_device_status;   // one per device; kernels OR their error bits
 constexpr int kMaxDevices = 64;
 struct DeviceInfo {
   int num_sms = 0;
-  int max_cluster = 8;     // largest thread-block cluster the decode kernel may use
   int* status = nullptr;
   bool ready = false;
 };
@@ -70,10 +69,6 @@ int device_info(DeviceInfo** out) {
     if (e != cudaSuccess) return fail_cuda(e, "cudaGetSymbolAddress(status)");
     d.num_sms = sms;
     d.status = static_cast<int*>(p);
-    if (const char* env = getenv("AWQ_MAX_CLUSTER")) {
-      int v = atoi(env);
-      if (v == 1 || v == 2 || v == 4 || v == 8 || v == 16) d.max_cluster = v;
-    }
     d.ready = true;
   }
   *out = &d;
@@ -127,11 +122,18 @@ int awq_dequant_f16(const int32_t* qweight, const int32_t* qzeros, const void* s
 size_t awq_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t group_size) {
   DeviceInfo* d = nullptr;
   if (device_info(&d)) return 0;
+  size_t need = 0;
   awq::GemvPlan plan;
-  if (!awq::plan_gemv(M, N, K, group_size, d->num_sms, true, &plan)) return 0;
-  size_t a = awq::gemv_workspace_bytes(plan);
-  // the unaligned (scalar-load) plan has the same grid, so the same size
-  return a;
+  // generic decode kernel (the unaligned, scalar-load plan has the same grid)
+  if (awq::plan_gemv(M, N, K, group_size, d->num_sms, true, &plan))
+    need = awq::gemv_workspace_bytes(plan);
+  // TMA decode kernel: launches of 16 tokens and one of the remainder
+  for (const int64_t mc : {M < 16 ? M : (int64_t)16, M > 16 ? M % 16 : (int64_t)0}) {
+    awq::GemvTmaPlan tp;
+    if (mc > 0 && awq::plan_gemv_tma(mc, N, K, group_size, d->num_sms, &tp) && tp.ws_bytes > need)
+      need = tp.ws_bytes;
+  }
+  return need;
 }
 
 int awq_workspace_init(void* workspace, size_t workspace_bytes, void* stream) {
@@ -183,13 +185,31 @@ int awq_gemm_f16_ex(const void* x, int64_t ldx, const int32_t* qweight, const in
     return AWQ_OK;
   }
 
-  const int max_cs = d->max_cluster;
-  if (awq::gemv_tma_supported(qweight, N, ldx, x) &&
-      awq::gemv_tma_smem_bytes(M, N, K, group_size, d->num_sms, max_cs) <= awq::kGemvTmaMaxSmem) {
-    cudaError_t e = awq::launch_gemv_tma(x, ldx, qweight, qzeros, scales, out, ldo, (int)M, (int)N,
-                                         (int)K, (int)group_size, d->num_sms, max_cs, d->status, st);
-    if (e != cudaSuccess) return fail_cuda(e, "decode (TMA) kernel launch");
-    return AWQ_OK;
+  if (awq::gemv_tma_supported(qweight, N, ldx, x)) {
+    // launches of at most 16 tokens (one plan for full chunks, one for the remainder)
+    awq::GemvTmaPlan full = {}, rest = {};
+    const int64_t m_full = M < 16 ? M : 16, m_rest = M > 16 ? M % 16 : 0;
+    const bool planned = awq::plan_gemv_tma(m_full, N, K, group_size, d->num_sms, &full) &&
+                         (m_rest == 0 || awq::plan_gemv_tma(m_rest, N, K, group_size, d->num_sms, &rest));
+    if (planned) {
+      size_t need = full.ws_bytes;
+      if (m_rest > 0 && rest.ws_bytes > need) need = rest.ws_bytes;
+      if (need > 0 && (!workspace || workspace_bytes < need))
+        return fail(AWQ_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+      if (need > 0 && !aligned16(workspace))
+        return fail(AWQ_ERR_INVALID_ARG, "workspace must be 16-byte aligned");
+      const char* xb = static_cast<const char*>(x);            // fp16 rows: 2 bytes each
+      char* ob = static_cast<char*>(out);
+      for (int64_t m0 = 0; m0 < M; m0 += 16) {
+        const int64_t mc = M - m0 < 16 ? M - m0 : 16;
+        cudaError_t e = awq::launch_gemv_tma(mc == m_full ? full : rest, xb + 2 * m0 * ldx, ldx,
+                                             qweight, qzeros, scales, ob + 2 * m0 * ldo, ldo, (int)mc,
+                                             (int)N, (int)K, (int)group_size, workspace, d->status,
+                                             st);
+        if (e != cudaSuccess) return fail_cuda(e, "decode (TMA) kernel launch");
+      }
+      return AWQ_OK;
+    }
   }
 
   const bool vec_ok = (N % 32 == 0) && aligned16(qweight);

@@ -38,11 +38,9 @@ constexpr int kGemvThreads = kGemvWarps * 32;
 constexpr int kStripN = 256;
 constexpr int kPrefetch = 4;     // blocks of 8 rows in flight per warp
 constexpr int kRedStride = 264;  // padded row of the cross-warp reduction buffer
-// Split-K arrival counters live in a fixed region at the head of the workspace, so a
-// call's fp32 partials (which follow the region) can never land on another call's
-// counters.  One launch uses at most kMaxCounters of them.
-constexpr int kMaxCounters = 16384;
-constexpr size_t kCounterRegionBytes = kMaxCounters * sizeof(int);
+// Split-K arrival counters live in a fixed region at the head of the workspace
+// (kCounterRegionBytes, awq_internal.h), so a call's fp32 partials (which follow the
+// region) can never land on another call's counters.
 
 __device__ __forceinline__ void mma_16816(float c[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                           uint32_t a3, uint32_t b0, uint32_t b1) {

@@ -1,15 +1,22 @@
-// awq_gemv_tma.cu -- decode AWQ W4A16 product (M <= 16 per token chunk), TMA-streamed,
-// cluster-reduced.  The fast path of the decode branch; awq_gemv.cu keeps the generic
-// kernel for shapes TMA cannot describe (N % 32 != 0, group_size % 32 != 0, unaligned).
+// awq_gemv_tma.cu -- decode AWQ W4A16 product (M <= 16 per launch), TMA-streamed, one
+// CTA per SM, deterministic split-K.  The fast path of the decode branch; awq_gemv.cu
+// keeps the generic kernel for shapes TMA cannot describe (N % 32 != 0,
+// group_size % 32 != 0, unaligned pointers).
 //
 // Replaces the M <= 4 dequant + torch.matmul branch of awq_gemm_forward
 // (songqiuyu/Qwen2-7B-Triton_Engine kernels/awq_gemm.py:251-266) and small-M calls
 // of _awq_gemm_kernel (kernels/awq_gemm.py:152-228).
 //
-// Roles (one CTA = 8 warps, one CTA per SM)
-//   every warp owns a contiguous, stage-aligned range of the CTA's K rows and a ring of
-//   shared-memory stages it refills itself: one 2-D TMA load of 32 K-rows x 32 packed
-//   words (4 KB, 128-byte swizzle) per stage, completing on the stage's mbarrier.  It
+// Work split
+//   An output tile is one 256-column strip of one chunk of 4 (M <= 4) or 8 tokens.  The
+//   grid has one CTA per SM whenever the tiles allow it: each tile gets `base` or
+//   `base + 1` CTAs, and each of those streams a contiguous, stage-aligned K range of
+//   the tile (the ranges of one tile differ by at most one 32-row stage), so every SM
+//   streams about the same number of bytes.
+// Roles (one CTA = 8 warps)
+//   every warp owns a contiguous, stage-aligned part of the CTA's K range and a ring of
+//   four 4 KB shared-memory stages it refills itself: one 2-D TMA load of 32 K-rows x 32
+//   packed words (128-byte swizzle) per stage, completing on the stage's mbarrier.  It
 //   walks its range one quantization group at a time; the inner loop over the group's
 //   stages is branch-free apart from the barrier wait and the refill: 4 x (2 shared
 //   loads + biased unpack + 8 mma.sync) per stage.  The group's zero/scale correction
@@ -17,19 +24,25 @@
 //   lane (g = lane/4, t = lane%4) reads rows t and t+4 of each 8-row block as 16 bytes
 //   from word chunk c(g) = (g >> 1) | ((g & 1) << 2); with the swizzle (chunk ^ row)
 //   the 8 lanes of each shared-memory phase hit 8 distinct 16-byte bank groups.
+// Prologue
+//   before griddepcontrol.wait (overlapping the previous kernel under programmatic
+//   launch): barrier set-up and an L2 prefetch of the CTA's first weight stages and of
+//   its zero / scale rows.  After it: one thread issues bulk copies of the activations
+//   and of the zero / scale rows into shared memory (two barriers: the loop starts on the
+//   activations alone), then every warp its first stages.
 // Math: dequantized pairs feed mma.sync.m16n8k16 (fp16 x fp16 -> fp32) with the
 //   activations spread over the (token, pair-slot) B columns.  For M <= 4 the MMA takes
 //   the exact biased values 1024 + w / 1024 + 16 w and the zero term
 //   (1024 + z) * sum(x) / (1024 + 16 z) * sum(x) is removed per group in fp32 before the
 //   fp32 scale (scale / 16) is applied; for M > 4 W is rounded to fp16 first exactly as
 //   the reference does.
-// Split-K: the CS CTAs of a thread-block cluster split K for one 256-column strip; each
-//   sums its 8 warps' partials in shared memory (one barrier, fixed order), then after a
-//   cluster barrier CTA r sums column slice r of all CS partials through distributed
-//   shared memory (fixed rank order, so the result is deterministic) and writes fp16.
-//   With CS = 1 the CTA writes its sum directly.  No global workspace, no atomics.
-// Every mbarrier wait is bounded (status word + early exit); both cluster barriers are
-// reached by every thread on every path, so a time-out never strands a peer CTA.
+// Split-K: each CTA sums its 8 warps' partials in shared memory (fixed order).  A tile
+//   with one CTA writes fp16 directly.  Otherwise each CTA writes an fp32 partial into
+//   its own workspace slot, and the last CTA of the tile to take a ticket (an atomic
+//   counter, which that CTA resets) sums the tile's slots in slot order --
+//   deterministic -- and writes fp16.
+// Every mbarrier wait is bounded (status word + early exit, after a bounded drain of
+// the copies still in flight).
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -50,15 +63,21 @@ constexpr int kRowsPerStage = 32;                 // four 8-row blocks per TMA c
 constexpr int kBlocksPerStage = kRowsPerStage / 8;
 constexpr int kStripN = 256;
 constexpr uint32_t kStageBytes = kRowsPerStage * 128;                // 4 KB
-constexpr int kRedStride = 264;
+// per-warp ring depth: 8 warps x 4 x 4 KB = 128 KB of weight copies in flight per SM.
+// One CTA per SM: with two, the block scheduler was seen packing two CTAs of one call
+// onto one SM while other SMs idled.
+constexpr int kStages = 4;
+constexpr uint32_t kRingBytes = kConsumers * kStages * kStageBytes;
+constexpr int kMaxSplits = 32;                    // CTAs per output tile, at most
+constexpr int kMinStagesPerCta = 2;               // K rows per CTA, at least 2 x 32
+// Weight stages per warp that are prefetched into L2 before the dependency wait.
+constexpr int kL2PrefetchStages = 2;
 
 template <int TOKSETS>
 struct DecGeo {
-  static constexpr int kStages = TOKSETS == 1 ? 4 : 2;              // per-warp ring depth
-  static constexpr uint32_t kRingBytes = kConsumers * kStages * kStageBytes;
   // row stride (floats) of a warp's partial sums parked in its own ring after the loop;
   // MP rows of it must fit the warp's kStages * 4 KB
-  static constexpr int kPartStride = TOKSETS == 1 ? kRedStride : kStripN;
+  static constexpr int kPartStride = TOKSETS == 1 ? 264 : kStripN;
   static_assert(4 * TOKSETS * kPartStride * 4 <= kStages * (int)kStageBytes, "partials fit the ring");
 };
 
@@ -69,11 +88,14 @@ struct TmaGemvArgs {
   const __half* scales;
   __half* out;
   int64_t ldo;
+  float* part;     // split-K partial slots [cta][MP][256] fp32 (null when no tile is split)
+  int* cnt;        // arrival counter per tile, zero between calls (null when no split)
   int M, N, K, gs, PN, KB;
-  int cs;          // CTAs per cluster (split-K factor)
-  int bps;         // 8-row blocks per CTA (multiple of kBlocksPerStage)
+  int strips;      // 256-column strips; tile = strip + strips * token chunk
+  int base, extra; // CTAs per tile: tiles [0, extra) get base + 1, the others base
   int xs_stride;   // halves per token row of xs
-  int ngrp_cta;    // quantization groups a CTA's K range can touch (zs / ss rows)
+  int xr;          // token rows reserved in xs
+  int ngrp_cta;    // zs / ss rows reserved (quantization groups a CTA's K range touches)
   int l2pf;        // weight stages each warp prefetches into L2 before the dependency wait
   int* status;
 };
@@ -97,35 +119,6 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
 __device__ __forceinline__ uint32_t lds_u16(uint32_t addr) {
   uint16_t v;
   asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
-  return v;
-}
-
-// 16-byte asynchronous global -> shared copy (no register round trip); completion is
-// awaited with cp_async_wait_all.
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.wait_all;" ::: "memory");
-}
-__device__ __forceinline__ void sts128_zero(uint32_t dst) {
-  asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(dst), "r"(0u) : "memory");
-}
-
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
-               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-__device__ __forceinline__ float ld_dsmem_f32(uint32_t local_addr, uint32_t rank) {
-  uint32_t remote;
-  float v;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
   return v;
 }
 
@@ -159,62 +152,109 @@ __global__ void __launch_bounds__(kThreads, 1)
 gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
   constexpr int MP = 4 * TOKSETS;
   constexpr bool BIAS = (TOKSETS == 1);
-  constexpr int kStages = DecGeo<TOKSETS>::kStages;
   extern __shared__ unsigned char smem_raw[];
   const uint32_t base_raw = sm100::smem_u32(smem_raw);
   const uint32_t sbase = (base_raw + 1023u) & ~1023u;
   unsigned char* sgen = smem_raw + (sbase - base_raw);
-  // layout: ring | red (MP x 264 fp32) | stage bars | abort | xs | zs | ss
-  const uint32_t off_red = DecGeo<TOKSETS>::kRingBytes;
-  const uint32_t off_full = off_red + MP * kRedStride * 4;
-  const uint32_t off_misc = off_full + kConsumers * kStages * 8;
+  // layout: ring | stage bars | staging bars (x, zeros + scales) | flags | xs | zs | ss
+  const uint32_t off_full = kRingBytes;
+  const uint32_t off_sbar = off_full + kConsumers * kStages * 8;
+  const uint32_t off_misc = off_sbar + 16;
   const uint32_t off_xs = off_misc + 16;
-  const uint32_t off_zs = off_xs + (uint32_t)MP * a.xs_stride * 2;
+  const uint32_t off_zs = off_xs + (uint32_t)a.xr * a.xs_stride * 2;
   const uint32_t off_ss = off_zs + (uint32_t)a.ngrp_cta * 128;
-  float* red = reinterpret_cast<float*>(sgen + off_red);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sgen + off_misc);
-  __half* xs = reinterpret_cast<__half*>(sgen + off_xs);
-  uint32_t* zs = reinterpret_cast<uint32_t*>(sgen + off_zs);    // [group][32 words]
-  __half* ss = reinterpret_cast<__half*>(sgen + off_ss);        // [group][256]
+  volatile int* last_flag = reinterpret_cast<volatile int*>(sgen + off_misc + 4);
+  const uint32_t xbar = sbase + off_sbar;          // activations staged
+  const uint32_t zbar = xbar + 8;                   // zero / scale rows staged
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
-  const int rank = (int)cluster_ctarank();          // == blockIdx.x (cluster spans x)
-  const int strip = blockIdx.y;
-  const int zc = blockIdx.z;
-  const int m0 = zc * MP;                           // token chunk of this CTA
+
+  // ---- this CTA's tile and K range -----------------------------------------------------
+  const int cta = blockIdx.x;
+  const int big = a.extra * (a.base + 1);
+  int tile, split, nsplit, first;
+  if (cta < big) {
+    tile = cta / (a.base + 1);
+    split = cta - tile * (a.base + 1);
+    nsplit = a.base + 1;
+    first = tile * (a.base + 1);
+  } else {
+    const int q = (cta - big) / a.base;
+    tile = a.extra + q;
+    split = cta - big - q * a.base;
+    nsplit = a.base;
+    first = big + q * a.base;
+  }
+  const int strip = tile % a.strips;
+  const int m0 = (tile / a.strips) * MP;            // token chunk of this CTA
   const int Mc = min(MP, a.M - m0);
-  const int cb0 = rank * a.bps;
-  const int cb1 = min(a.KB, cb0 + a.bps);
-  const int nb = max(0, cb1 - cb0);
+  const int nstage_tile = a.KB / kBlocksPerStage;
+  const int st0 = (int)((int64_t)split * nstage_tile / nsplit);
+  const int st1 = (int)((int64_t)(split + 1) * nstage_tile / nsplit);
+  const int cb0 = st0 * kBlocksPerStage;
+  const int nb = (st1 - st0) * kBlocksPerStage;
   const int krow0 = cb0 * 8;
   const int Kc = nb * 8;
+  const int g0 = krow0 / a.gs;
+  const int ng = Kc > 0 ? (krow0 + Kc - 1) / a.gs - g0 + 1 : 0;
+  const uint32_t zbytes = (uint32_t)min(32, a.PN - strip * 32) * 4u;      // multiple of 16
+  const uint32_t sbytes = (uint32_t)min(kStripN, a.N - strip * kStripN) * 2u;
   auto full_bar = [&](int w, int s) { return sbase + off_full + (uint32_t)(w * kStages + s) * 8u; };
   auto stage_addr = [&](int w, int s) {
     return sbase + (uint32_t)(w * kStages + s) * kStageBytes;
   };
 
-  // every warp initialises its own stage barriers and starts its own stream
   int b0, b1;
   warp_range(cb0, nb, warp, b0, b1);
   const int nst = (b1 - b0) / kBlocksPerStage;
   if (lane == 0) {
     for (int s2 = 0; s2 < kStages; ++s2) sm100::mbar_init(full_bar(warp, s2), 1);
-    sm100::fence_mbar_init();
     if (warp == 0) {
+      sm100::mbar_init(xbar, 1);
+      sm100::mbar_init(zbar, 1);
       *abort_flag = 0;
       sm100::prefetch_tmap(&tmW);
     }
-    // Under programmatic dependent launch this part overlaps the previous kernel: an L2
-    // prefetch of the first weight stages is safe before the dependency is resolved
-    // (L2 stays coherent with the previous kernel's writes); the copies into shared
-    // memory are issued only after griddepcontrol.wait.
-    for (int j = 0; j < a.l2pf && j < nst; ++j)
-      sm100::tma_prefetch_l2_2d(&tmW, strip * 32, (b0 + j * kBlocksPerStage) * 8);
+    sm100::fence_mbar_init();
+  }
+  // ---- before the dependency wait: warm L2 with this CTA's first weight stages and its
+  // zero / scale rows.  These are read-only inputs, and a prefetch only fills L2 -- the
+  // coherence point -- so it never hands the kernel a stale value; everything that lands
+  // in registers or shared memory is read after griddepcontrol.wait.
+  for (int j = lane; j < a.l2pf && j < nst; j += 32)
+    sm100::tma_prefetch_l2_2d(&tmW, strip * 32, (b0 + j * kBlocksPerStage) * 8);
+  if (a.l2pf > 0) {
+    for (int i = tid; i < 2 * ng; i += kThreads) {
+      const int gi = i >> 1;
+      if (i & 1)
+        sm100::bulk_prefetch_l2(a.scales + (int64_t)(g0 + gi) * a.N + strip * kStripN, sbytes);
+      else
+        sm100::bulk_prefetch_l2(a.qz + (int64_t)(g0 + gi) * a.PN + strip * 32, zbytes);
+    }
   }
   sm100::grid_dependency_wait();        // no-op unless launched as a programmatic dependent
   sm100::grid_launch_dependents();
+
+  // ---- staging: activations xs[m][k] (Mc rows), then the strip's zero / scale rows, as
+  // bulk copies issued ahead of the weight stages so that they are not queued behind
+  // them.  The main loop needs only the activations to start; for M <= 4 the zero /
+  // scale rows are first read at the end of the first group segment.
+  if (tid == 0) {
+    sm100::mbar_arrive_expect_tx(xbar, (uint32_t)Mc * (uint32_t)Kc * 2u);
+    for (int m = 0; m < Mc; ++m)
+      sm100::bulk_load(sbase + off_xs + (uint32_t)(m * a.xs_stride) * 2u,
+                       a.x + (int64_t)(m0 + m) * a.ldx + krow0, (uint32_t)Kc * 2u, xbar);
+    sm100::mbar_arrive_expect_tx(zbar, (uint32_t)ng * (zbytes + sbytes));
+    for (int gi = 0; gi < ng; ++gi) {
+      sm100::bulk_load(sbase + off_zs + (uint32_t)gi * 128u,
+                       a.qz + (int64_t)(g0 + gi) * a.PN + strip * 32, zbytes, zbar);
+      sm100::bulk_load(sbase + off_ss + (uint32_t)gi * (kStripN * 2u),
+                       a.scales + (int64_t)(g0 + gi) * a.N + strip * kStripN, sbytes, zbar);
+    }
+  }
   __syncwarp();
   if (lane == 0) {
     for (int j = 0; j < kStages && j < nst; ++j) {
@@ -223,40 +263,10 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
                          (b0 + j * kBlocksPerStage) * 8);
     }
   }
-
-  // ---- stage activations xs[m][k] and the strip's zeros / scales ---------------------
-  // asynchronous 16-byte copies: every thread's copies are in flight at once, so the
-  // staging costs one memory round trip (it overlaps the first weight stages)
-  {
-    const int vecs = Kc / 8;                         // 16-byte vectors per token row
-    for (int i = tid; i < MP * vecs; i += kThreads) {
-      const int m = i / vecs, v = i - m * vecs;
-      const uint32_t dst = sbase + off_xs + (uint32_t)(m * a.xs_stride + v * 8) * 2u;
-      if (m < Mc)
-        cp_async16(dst, a.x + (int64_t)(m0 + m) * a.ldx + krow0 + v * 8);
-      else
-        sts128_zero(dst);
-    }
-    const int g0 = krow0 / a.gs;
-    const int ng = Kc > 0 ? (krow0 + Kc - 1) / a.gs - g0 + 1 : 0;
-    for (int i = tid; i < ng * 40; i += kThreads) {
-      const int gi = i / 40, v = i - gi * 40;      // 8 vectors of zeros, 32 of scales
-      if (v < 8) {
-        const int wc = strip * 32 + v * 4;
-        const uint32_t dst = sbase + off_zs + (uint32_t)(gi * 128 + v * 16);
-        if (wc < a.PN) cp_async16(dst, a.qz + (int64_t)(g0 + gi) * a.PN + wc);
-        else sts128_zero(dst);
-      } else {
-        const int n = strip * kStripN + (v - 8) * 8;
-        const uint32_t dst = sbase + off_ss + (uint32_t)(gi * kStripN * 2 + (v - 8) * 16);
-        if (n < a.N) cp_async16(dst, a.scales + (int64_t)(g0 + gi) * a.N + n);
-        else sts128_zero(dst);
-      }
-    }
-    cp_async_wait_all();
-  }
-  __syncthreads();
-  const int grp0 = krow0 / a.gs;
+  __syncthreads();                                   // staging barriers initialised for all
+  bool ok = sm100::mbar_wait_bounded(xbar, 0, a.status);
+  bool zs_ready = false;                             // zbar waited by this thread
+  if (!BIAS && ok) ok = zs_ready = sm100::mbar_wait_bounded(zbar, 0, a.status);
 
   const int chunk = (g >> 1) | ((g & 1) << 2);       // conflict-free word chunk
   float acc[TOKSETS][8][4];
@@ -267,24 +277,28 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[s2][q][i] = 0.f;
 
+  int j = 0;                                          // stage counter of this warp
   {
     const uint32_t bsel = (g & 1) ? 0x1054u : 0x5410u;   // x into this lane's pair slot
     const uint32_t lane_off_a = (uint32_t)t * 128u + ((uint32_t)(chunk ^ t) << 4);
     const uint32_t lane_off_b = (uint32_t)(t + 4) * 128u + ((uint32_t)(chunk ^ (t + 4)) << 4);
     // shared-memory byte address of x[token][k = 0] for this lane's tokens (k is added
-    // per block); explicit ld.shared keeps these loads off the L1TEX path
+    // per block); a token beyond the chunk's Mc rows reads row 0 and is masked to zero
     uint32_t xrow[TOKSETS];
+    uint32_t xmask[TOKSETS];
 #pragma unroll
-    for (int s2 = 0; s2 < TOKSETS; ++s2)
-      xrow[s2] = sbase + off_xs + (uint32_t)(((4 * s2 + (g >> 1)) * a.xs_stride + t - krow0) * 2);
+    for (int s2 = 0; s2 < TOKSETS; ++s2) {
+      const int m = 4 * s2 + (g >> 1);
+      const bool live = m < Mc;
+      xmask[s2] = live ? 0xffffffffu : 0u;
+      xrow[s2] = sbase + off_xs + (uint32_t)(((live ? m : 0) * a.xs_stride + t - krow0) * 2);
+    }
     uint32_t zcst[4][4], scl[4][4];
     float pacc[BIAS ? 8 : 1][4];
-    int j = 0;                                          // stage counter of this warp
-    bool ok = true;
     for (int kb = b0 * 8; kb < b1 * 8 && ok;) {
       const int grp = kb / a.gs;
       const int kend = min(b1 * 8, (grp + 1) * a.gs);
-      const int gl = grp - grp0;
+      const int gl = grp - g0;
       if constexpr (!BIAS) {
         // fp16 W path: zeros and scales are used per weight
         const uint4 z4 = lds128(sbase + off_zs + (uint32_t)(gl * 128 + chunk * 16));
@@ -319,8 +333,8 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
 #pragma unroll
           for (int s2 = 0; s2 < TOKSETS; ++s2) {
             const uint32_t xa = xrow[s2] + (uint32_t)(krow + h * 8) * 2u;
-            bf0[s2] = prmt(lds_u16(xa), 0u, bsel);
-            bf1[s2] = prmt(lds_u16(xa + 8u), 0u, bsel);
+            bf0[s2] = prmt(lds_u16(xa), 0u, bsel) & xmask[s2];
+            bf1[s2] = prmt(lds_u16(xa + 8u), 0u, bsel) & xmask[s2];
           }
           const uint32_t wa[4] = {va.x, va.y, va.z, va.w};
           const uint32_t wb[4] = {vb.x, vb.y, vb.z, vb.w};
@@ -360,16 +374,26 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
       }
       if constexpr (BIAS) {
         // close the group segment [kb, kend): remove the zero term, apply the scale
+        if (!zs_ready) {
+          if (!sm100::mbar_wait_bounded(zbar, 0, a.status)) {
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          zs_ready = true;
+        }
         float part = 0.f;
-        const int u0 = (kb - krow0) >> 3, u1 = (kend - krow0) >> 3;
-        const uint32_t xt = sbase + off_xs + (uint32_t)(t * a.xs_stride) * 2u;
-        for (int u = u0 + g; u < u1; u += 8) {
-          const uint4 v = lds128(xt + (uint32_t)u * 16u);
-          const uint32_t hv[4] = {v.x, v.y, v.z, v.w};
+        if (t < Mc) {
+          const int u0 = (kb - krow0) >> 3, u1 = (kend - krow0) >> 3;
+          const uint32_t xt = sbase + off_xs + (uint32_t)(t * a.xs_stride) * 2u;
+          for (int u = u0 + g; u < u1; u += 8) {
+            const uint4 v = lds128(xt + (uint32_t)u * 16u);
+            const uint32_t hv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const float2 f = __half22float2(u32_as_h2(hv[k]));
-            part += f.x + f.y;
+            for (int k = 0; k < 4; ++k) {
+              const float2 f = __half22float2(u32_as_h2(hv[k]));
+              part += f.x + f.y;
+            }
           }
         }
         part += __shfl_xor_sync(0xffffffffu, part, 4);
@@ -402,14 +426,19 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
       }
       kb = kend;
     }
-    if (!ok && lane == 0) {
-      // a stage never arrived: wait (bounded) for this warp's copies still in flight
-      for (int jj = j; jj < nst && jj < j + kStages; ++jj)
-        sm100::mbar_wait_bounded(full_bar(warp, jj % kStages), (jj / kStages) & 1, nullptr,
-                                 50000000ull);
-    }
-    __syncwarp();
   }
+  if (!ok && lane == 0) {
+    // a copy never arrived: wait (bounded) for this warp's copies still in flight, and
+    // for the staging copies
+    for (int jj = j; jj < nst && jj < j + kStages; ++jj)
+      sm100::mbar_wait_bounded(full_bar(warp, jj % kStages), (jj / kStages) & 1, nullptr,
+                               50000000ull);
+    if (warp == 0) {
+      sm100::mbar_wait_bounded(xbar, 0, nullptr, 50000000ull);
+      sm100::mbar_wait_bounded(zbar, 0, nullptr, 50000000ull);
+    }
+  }
+  __syncwarp();
 
   // ---- CTA reduction: each warp parks its partial in its own (now idle) ring, one
   // barrier, then the 8 partials are summed in warp order -------------------------------
@@ -426,36 +455,48 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
   }
   __syncthreads();
   const int nbase = strip * kStripN;
-  for (int idx = tid; idx < MP * kStripN; idx += kThreads) {
+  const size_t slot_stride = (size_t)MP * kStripN;
+  for (int idx = tid; idx < Mc * kStripN; idx += kThreads) {
     const int m = idx / kStripN, nl = idx - m * kStripN;
     float v = 0.f;
 #pragma unroll
     for (int w = 0; w < kConsumers; ++w)
       v += reinterpret_cast<const float*>(sgen + (uint32_t)w * kStages * kStageBytes)
                [m * DecGeo<TOKSETS>::kPartStride + nl];
-    if (a.cs == 1) {
+    if (nsplit == 1) {
       const int n = nbase + nl;
-      if (m < Mc && n < a.N) a.out[(int64_t)(m0 + m) * a.ldo + n] = __float2half_rn(v);
+      if (n < a.N) a.out[(int64_t)(m0 + m) * a.ldo + n] = __float2half_rn(v);
     } else {
-      red[m * kRedStride + nl] = v;
+      a.part[(size_t)cta * slot_stride + idx] = v;
     }
   }
-  if (a.cs == 1) return;                               // grid-uniform: no cluster to serve
+  if (nsplit == 1) return;                             // uniform over the CTA
 
-  // ---- cluster reduction over distributed shared memory ----------------------------
-  cluster_sync_all();                                  // every CTA's red is complete
-  const int cw = kStripN / a.cs;                       // columns reduced by this CTA
-  const uint32_t red_addr = sbase + off_red;
-  for (int idx = tid; idx < Mc * cw; idx += kThreads) {
-    const int m = idx / cw;
-    const int nl = rank * cw + (idx - m * cw);
-    const uint32_t la = red_addr + (uint32_t)(m * kRedStride + nl) * 4u;
-    float v = 0.f;
-    for (int r = 0; r < a.cs; ++r) v += ld_dsmem_f32(la, (uint32_t)r);
+  // ---- split-K: ticket, then the last CTA of the tile sums the slots in order --------
+  __threadfence();                                     // this thread's slot stores first
+  __syncthreads();
+  if (tid == 0) *last_flag = (atomicAdd(a.cnt + tile, 1) == nsplit - 1) ? 1 : 0;
+  __syncthreads();
+  if (!*last_flag) return;
+  __threadfence();
+  for (int idx = tid; idx < Mc * kStripN; idx += kThreads) {
+    const int m = idx / kStripN, nl = idx - m * kStripN;
     const int n = nbase + nl;
-    if (n < a.N) a.out[(int64_t)(m0 + m) * a.ldo + n] = __float2half_rn(v);
+    if (n >= a.N) continue;
+    const float* p = a.part + (size_t)first * slot_stride + idx;
+    float v = 0.f;
+    for (int r0 = 0; r0 < nsplit; r0 += 8) {
+      float v8[8];
+#pragma unroll
+      for (int r = 0; r < 8; ++r)                      // independent loads in flight together
+        v8[r] = (r0 + r < nsplit) ? __ldcg(p + (size_t)(r0 + r) * slot_stride) : 0.f;
+#pragma unroll
+      for (int r = 0; r < 8; ++r)
+        if (r0 + r < nsplit) v += v8[r];               // slot order: deterministic
+    }
+    a.out[(int64_t)(m0 + m) * a.ldo + n] = __float2half_rn(v);
   }
-  cluster_sync_all();                                  // keep smem alive for the readers
+  if (tid == 0) a.cnt[tile] = 0;                       // ready for the next call
 }
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -476,119 +517,107 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-struct TmaPlan {
-  int cs, bps, xs_stride, ngrp, toksets;
-  size_t smem;
-};
-
-template <int TOKSETS>
-size_t smem_bytes(int xs_stride, int ngrp) {
-  const int MP = 4 * TOKSETS;
-  constexpr int S = DecGeo<TOKSETS>::kStages;
-  return 1024 + DecGeo<TOKSETS>::kRingBytes + (size_t)MP * kRedStride * 4 +
-         kConsumers * S * 8 + 16 + (size_t)MP * xs_stride * 2 + (size_t)ngrp * (128 + kStripN * 2);
+size_t smem_bytes(int xr, int xs_stride, int ngrp) {
+  return 1024 + kRingBytes + kConsumers * kStages * 8 + 16 + 16 + (size_t)xr * xs_stride * 2 +
+         (size_t)ngrp * (128 + kStripN * 2);
 }
 
-// Cluster size: grow the split-K factor while the grid stays within one CTA per SM and
-// every consumer warp keeps at least two stages; then grow it further (up to max_cs)
-// if the CTA's staged activations do not fit in shared memory.
-bool plan_tma(int64_t M, int64_t N, int64_t K, int64_t gs, int num_sms, int max_cs, TmaPlan* p) {
-  if (N % 32 || gs % kRowsPerStage || K % gs) return false;
-  const int64_t strips = (N + kStripN - 1) / kStripN;
-  // M <= 4: one 4-token set; otherwise chunks of 8 tokens (two sets) per CTA row of the
-  // grid -- 16 tokens per CTA would need more registers than 9 warps per SM allow
-  p->toksets = M <= 4 ? 1 : 2;
-  const int64_t zchunks = (M + 4 * p->toksets - 1) / (4 * p->toksets);
-  const int64_t KB = K / 8;
-  int cs = 1;
-  while (cs < max_cs && strips * zchunks * cs * 2 <= (int64_t)num_sms &&
-         KB / (cs * 2) >= (int64_t)kConsumers * kBlocksPerStage * 2)
-    cs *= 2;
-  for (;; cs *= 2) {
-    int bps = (int)((KB + cs - 1) / cs);
-    bps = (bps + kBlocksPerStage - 1) / kBlocksPerStage * kBlocksPerStage;
-    const int xs_stride = bps * 8 + 8;                // +16 B staggers token rows
-    const int ngrp = (int)((bps * 8 + gs - 1) / gs) + 1;
-    size_t smem = p->toksets == 1 ? smem_bytes<1>(xs_stride, ngrp) : smem_bytes<2>(xs_stride, ngrp);
-    if (smem <= kGemvTmaMaxSmem) {
-      p->cs = cs; p->bps = bps; p->xs_stride = xs_stride; p->ngrp = ngrp; p->smem = smem;
-      return true;
-    }
-    if (cs >= max_cs) return false;
-  }
-}
-
-// Programmatic dependent launch is off unless AWQ_PDL=1 (read once per process): on the
-// mixed decode stack it measured slower than plain stream order.
+// Programmatic dependent launch is on unless AWQ_PDL=0 (read once per process): the
+// next call's CTAs then become resident while this one streams, set up their barriers
+// and warm L2 before the dependency is resolved.
 bool pdl_enabled() {
   static int v = -1;
   if (v < 0) {
     const char* e = getenv("AWQ_PDL");
-    v = (e && e[0] == '1') ? 1 : 0;
+    v = (e && e[0] == '0') ? 0 : 1;
   }
   return v == 1;
 }
 
 template <int TOKSETS>
-cudaError_t launch_t(const CUtensorMap& tm, const TmaGemvArgs& a, int strips, int zchunks,
-                     size_t smem, cudaStream_t stream) {
+cudaError_t launch_t(const CUtensorMap& tm, const TmaGemvArgs& a, int grid, size_t smem,
+                     cudaStream_t stream) {
   static std::once_flag once;
   static cudaError_t attr = cudaSuccess;
   std::call_once(once, [] {
     attr = cudaFuncSetAttribute(gemv_tma_kernel<TOKSETS>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemvTmaMaxSmem);
-    if (attr == cudaSuccess)
-      attr = cudaFuncSetAttribute(gemv_tma_kernel<TOKSETS>,
-                                  cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   });
   if (attr != cudaSuccess) return attr;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.cs, strips, zchunks);
+  cfg.gridDim = dim3(grid, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute at[2];
-  at[0].id = cudaLaunchAttributeClusterDimension;
-  at[0].val.clusterDim.x = a.cs;
-  at[0].val.clusterDim.y = 1;
-  at[0].val.clusterDim.z = 1;
   // programmatic dependent launch: the kernel waits (griddepcontrol.wait) before it
   // touches anything the previous grid may write
-  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  at[1].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
-  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, gemv_tma_kernel<TOKSETS>, tm, a);
 }
 
 }  // namespace
+
+// One CTA per SM when the tiles allow it (each CTA gets at least kMinStagesPerCta
+// stages, a tile at most kMaxSplits CTAs); one more CTA per tile at a time while the
+// largest K range's staged activations and zero / scale rows do not fit in shared memory.
+bool plan_gemv_tma(int64_t M, int64_t N, int64_t K, int64_t gs, int num_sms, GemvTmaPlan* p) {
+  if (M <= 0 || M > 16 || N <= 0 || N % 32 || gs % kRowsPerStage || K <= 0 || K % gs ||
+      num_sms <= 0)
+    return false;
+  const int toksets = M <= 4 ? 1 : 2;
+  const int64_t MP = 4 * toksets;
+  const int64_t strips = (N + kStripN - 1) / kStripN;
+  const int64_t tiles = strips * ((M + MP - 1) / MP);
+  const int64_t nstage = K / kRowsPerStage;                   // stages per tile
+  int64_t grid0 = tiles;
+  if (tiles < num_sms) {
+    int64_t maxc = nstage / kMinStagesPerCta;
+    if (maxc > kMaxSplits) maxc = kMaxSplits;
+    if (maxc < 1) maxc = 1;
+    grid0 = tiles * maxc < num_sms ? tiles * maxc : num_sms;
+  }
+  const int xr = toksets == 1 ? (int)M : 8;
+  for (int64_t grid = grid0;; grid += tiles) {
+    const int64_t b = grid / tiles, extra = grid % tiles;   // CTAs per tile: b or b + 1
+    if (b > nstage || grid > 0x7fffffff) return false;
+    const int64_t kc_max = (nstage + b - 1) / b * kRowsPerStage;   // rows of the largest range
+    const int xs_stride = (int)kc_max + 8;                          // +16 B staggers token rows
+    const int ngrp = (int)(kc_max / gs) + 2;
+    const size_t smem = smem_bytes(xr, xs_stride, ngrp);
+    if (smem > kGemvTmaMaxSmem) continue;
+    const bool split = b > 1 || extra > 0;
+    if (split && tiles > kMaxCounters) return false;
+    p->toksets = toksets;
+    p->strips = (int)strips;
+    p->tiles = (int)tiles;
+    p->grid = (int)grid;
+    p->base = (int)b;
+    p->extra = (int)extra;
+    p->xr = xr;
+    p->xs_stride = xs_stride;
+    p->ngrp = ngrp;
+    p->smem = smem;
+    p->ws_bytes = split ? kCounterRegionBytes + (size_t)grid * MP * kStripN * sizeof(float) : 0;
+    return true;
+  }
+}
 
 bool gemv_tma_supported(const int32_t* qweight, int64_t N, int64_t ldx, const void* x) {
   return (N % 32 == 0) && ((reinterpret_cast<uintptr_t>(qweight) & 15) == 0) &&
          ((reinterpret_cast<uintptr_t>(x) & 15) == 0) && (ldx % 8 == 0) && encode_fn() != nullptr;
 }
 
-int gemv_tma_cluster_size(int64_t M, int64_t N, int64_t K, int num_sms, int max_cs) {
-  TmaPlan p;
-  if (!plan_tma(M, N, K, 128, num_sms, max_cs, &p)) return 0;
-  return p.cs;
-}
-
-size_t gemv_tma_smem_bytes(int64_t M, int64_t N, int64_t K, int64_t group_size, int num_sms,
-                           int max_cs) {
-  TmaPlan p;
-  if (!plan_tma(M, N, K, group_size, num_sms, max_cs, &p)) return (size_t)-1;
-  return p.smem;
-}
-
-cudaError_t launch_gemv_tma(const void* x, int64_t ldx, const int32_t* qweight,
-                            const int32_t* qzeros, const void* scales, void* out, int64_t ldo,
-                            int M, int N, int K, int group_size, int num_sms, int max_cs,
-                            int* dev_status, cudaStream_t stream) {
+cudaError_t launch_gemv_tma(const GemvTmaPlan& p, const void* x, int64_t ldx,
+                            const int32_t* qweight, const int32_t* qzeros, const void* scales,
+                            void* out, int64_t ldo, int M, int N, int K, int group_size,
+                            void* workspace, int* dev_status, cudaStream_t stream) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return cudaErrorNotSupported;
-  TmaPlan p;
-  if (!plan_tma(M, N, K, group_size, num_sms, max_cs, &p)) return cudaErrorInvalidValue;
+  if (p.ws_bytes > 0 && !workspace) return cudaErrorInvalidValue;
   CUtensorMap tm;
   cuuint64_t dims[2] = {(cuuint64_t)(N / 8), (cuuint64_t)K};
   cuuint64_t strides[1] = {(cuuint64_t)N / 2};
@@ -598,32 +627,28 @@ cudaError_t launch_gemv_tma(const void* x, int64_t ldx, const int32_t* qweight,
           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return cudaErrorInvalidValue;
-  const int strips = (N + kStripN - 1) / kStripN;
   TmaGemvArgs a;
+  a.x = static_cast<const __half*>(x);
   a.ldx = ldx;
   a.qz = qzeros;
   a.scales = static_cast<const __half*>(scales);
+  a.out = static_cast<__half*>(out);
   a.ldo = ldo;
-  a.N = N; a.K = K; a.gs = group_size; a.PN = N / 8; a.KB = K / 8;
-  a.cs = p.cs;
-  a.bps = p.bps;
+  a.cnt = p.ws_bytes > 0 ? static_cast<int*>(workspace) : nullptr;
+  a.part = p.ws_bytes > 0
+               ? reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + kCounterRegionBytes)
+               : nullptr;
+  a.M = M; a.N = N; a.K = K; a.gs = group_size; a.PN = N / 8; a.KB = K / 8;
+  a.strips = p.strips;
+  a.base = p.base;
+  a.extra = p.extra;
   a.xs_stride = p.xs_stride;
+  a.xr = p.xr;
   a.ngrp_cta = p.ngrp;
-  a.l2pf = pdl_enabled() ? 4 : 0;
+  a.l2pf = pdl_enabled() ? kL2PrefetchStages : 0;
   a.status = dev_status;
-  const int64_t chunk = 4 * p.toksets;                 // tokens per CTA row of the grid
-  const int64_t max_rows = (int64_t)65535 * chunk;
-  for (int64_t m0 = 0; m0 < M; m0 += max_rows) {
-    const int64_t rows = (M - m0 < max_rows) ? (M - m0) : max_rows;
-    a.x = static_cast<const __half*>(x) + m0 * ldx;
-    a.out = static_cast<__half*>(out) + m0 * ldo;
-    a.M = (int)rows;
-    const int z = (int)((rows + chunk - 1) / chunk);
-    cudaError_t e = p.toksets == 1 ? launch_t<1>(tm, a, strips, z, p.smem, stream)
-                                   : launch_t<2>(tm, a, strips, z, p.smem, stream);
-    if (e != cudaSuccess) return e;
-  }
-  return cudaSuccess;
+  return p.toksets == 1 ? launch_t<1>(tm, a, p.grid, p.smem, stream)
+                        : launch_t<2>(tm, a, p.grid, p.smem, stream);
 }
 
 }  // namespace awq

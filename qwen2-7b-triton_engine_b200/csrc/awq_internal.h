@@ -13,6 +13,12 @@ cudaError_t launch_dequant(const int32_t* qweight, const int32_t* qzeros, const 
                            void* out, int64_t K, int64_t N, int64_t group_size, int num_sms,
                            cudaStream_t stream);
 
+// Split-K arrival counters sit at the head of the caller's workspace (the generic and
+// the TMA decode kernels share the region); every kernel leaves the counters it used at
+// zero.  One launch uses at most kMaxCounters of them.
+constexpr int kMaxCounters = 16384;
+constexpr size_t kCounterRegionBytes = kMaxCounters * sizeof(int);
+
 // ---- decode / skinny GEMM on mma.sync (awq_gemv.cu) ----------------------------------
 struct GemvPlan {
   int strips;      // ceil(N / 256): one warp-wide strip of 32 packed words each
@@ -38,16 +44,28 @@ cudaError_t launch_gemv(const GemvPlan& plan, const void* x, int64_t ldx, const 
                         const int32_t* qzeros, const void* scales, void* out, int64_t ldo, int M,
                         int N, int K, int group_size, void* workspace, cudaStream_t stream);
 
-// ---- decode on mma.sync with TMA streaming and cluster split-K (awq_gemv_tma.cu) -------
+// ---- decode on mma.sync with TMA streaming, one CTA per SM (awq_gemv_tma.cu) ---------
 // Shapes TMA can describe (N % 32 == 0, 16-byte aligned qweight and x, ldx % 8 == 0).
 bool gemv_tma_supported(const int32_t* qweight, int64_t N, int64_t ldx, const void* x);
-size_t gemv_tma_smem_bytes(int64_t M, int64_t N, int64_t K, int64_t group_size, int num_sms,
-                           int max_cs);
-int gemv_tma_cluster_size(int64_t M, int64_t N, int64_t K, int num_sms, int max_cs);
-cudaError_t launch_gemv_tma(const void* x, int64_t ldx, const int32_t* qweight,
-                            const int32_t* qzeros, const void* scales, void* out, int64_t ldo,
-                            int M, int N, int K, int group_size, int num_sms, int max_cs,
-                            int* dev_status, cudaStream_t stream);
+struct GemvTmaPlan {
+  int toksets;     // 4-token sets per CTA: 1 (M <= 4) or 2
+  int strips;      // 256-column strips
+  int tiles;       // strips x token chunks
+  int grid;        // CTAs
+  int base, extra; // CTAs per tile: the first `extra` tiles get base + 1, the rest base
+  int xr;          // token rows reserved in shared memory
+  int xs_stride;   // halves per staged token row
+  int ngrp;        // zero / scale rows reserved in shared memory
+  size_t smem;     // dynamic shared memory per CTA
+  size_t ws_bytes; // workspace (counter region + fp32 split-K slots); 0 when no tile splits
+};
+// Plan of one launch of at most 16 tokens; false when the shape cannot be planned.
+bool plan_gemv_tma(int64_t M, int64_t N, int64_t K, int64_t group_size, int num_sms,
+                   GemvTmaPlan* plan);
+cudaError_t launch_gemv_tma(const GemvTmaPlan& plan, const void* x, int64_t ldx,
+                            const int32_t* qweight, const int32_t* qzeros, const void* scales,
+                            void* out, int64_t ldo, int M, int N, int K, int group_size,
+                            void* workspace, int* dev_status, cudaStream_t stream);
 constexpr size_t kGemvTmaMaxSmem = 200 * 1024;
 
 // ---- prefill GEMM on tcgen05 / TMEM (awq_gemm_tc.cu) ----------------------------------

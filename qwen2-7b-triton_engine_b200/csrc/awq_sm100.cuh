@@ -77,6 +77,19 @@ __device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int c
   asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];"
                ::"l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1) : "memory");
 }
+// Contiguous global -> shared copy of `bytes` (both addresses 16-byte aligned, size a
+// multiple of 16) that completes on mbarrier `bar` as transaction bytes.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
+                                          uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+// L2 prefetch of `bytes` contiguous bytes (address 16-byte aligned, size a multiple of 16).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
 // Programmatic dependent launch: wait until the preceding grid in the stream has
 // completed and its writes are visible; allow the next grid to start launching.
 __device__ __forceinline__ void grid_dependency_wait() {
