@@ -15,10 +15,10 @@
 //   streams about the same number of bytes.
 // Roles (one CTA = 8 warps)
 //   every warp owns a contiguous, stage-aligned part of the CTA's K range and a ring of
-//   four 4 KB shared-memory stages it refills itself: one 2-D TMA load of 32 K-rows x 32
+//   two 8 KB shared-memory stages it refills itself: one 2-D TMA load of 64 K-rows x 32
 //   packed words (128-byte swizzle) per stage, completing on the stage's mbarrier.  It
 //   walks its range one quantization group at a time; the inner loop over the group's
-//   stages is branch-free apart from the barrier wait and the refill: 4 x (2 shared
+//   stages is branch-free apart from the barrier wait and the refill: 8 x (2 shared
 //   loads + biased unpack + 8 mma.sync) per stage.  The group's zero/scale correction
 //   runs once per group, outside that loop.
 //   lane (g = lane/4, t = lane%4) reads rows t and t+4 of each 8-row block as 16 bytes
@@ -26,10 +26,10 @@
 //   the 8 lanes of each shared-memory phase hit 8 distinct 16-byte bank groups.
 // Prologue
 //   before griddepcontrol.wait (overlapping the previous kernel under programmatic
-//   launch): barrier set-up and an L2 prefetch of the CTA's first weight stages and of
-//   its zero / scale rows.  After it: one thread issues bulk copies of the activations
-//   and of the zero / scale rows into shared memory (two barriers: the loop starts on the
-//   activations alone), then every warp its first stages.
+//   launch): barrier set-up and an L2 prefetch of every warp's first weight stages.
+//   After it: all threads cp.async-copy the activations into shared memory, every warp
+//   issues its first weight stages and cp.async-copies the zero / scale rows of its own
+//   groups; the loop starts on the activations alone.
 // Math: dequantized pairs feed mma.sync.m16n8k16 (fp16 x fp16 -> fp32) with the
 //   activations spread over the (token, pair-slot) B columns.  For M <= 4 the MMA takes
 //   the exact biased values 1024 + w / 1024 + 16 w and the zero term
@@ -59,17 +59,18 @@ namespace {
 
 constexpr int kConsumers = 8;                     // warps per CTA
 constexpr int kThreads = kConsumers * 32;
-constexpr int kRowsPerStage = 32;                 // four 8-row blocks per TMA copy
+constexpr int kRowsPerStage = 64;                 // eight 8-row blocks per TMA copy
 constexpr int kBlocksPerStage = kRowsPerStage / 8;
 constexpr int kStripN = 256;
-constexpr uint32_t kStageBytes = kRowsPerStage * 128;                // 4 KB
-// per-warp ring depth: 8 warps x 4 x 4 KB = 128 KB of weight copies in flight per SM.
-// One CTA per SM: with two, the block scheduler was seen packing two CTAs of one call
-// onto one SM while other SMs idled.
-constexpr int kStages = 4;
+constexpr uint32_t kStageBytes = kRowsPerStage * 128;                // 8 KB
+// per-warp ring depth: 8 warps x 2 x 8 KB = 128 KB of weight copies in flight per SM.
+// 8 KB copies: the TMA unit's cost per copy made 4 KB copies measurably slower.  One CTA
+// per SM: with two, the block scheduler was seen packing two CTAs of one call onto one
+// SM while other SMs idled.
+constexpr int kStages = 2;
 constexpr uint32_t kRingBytes = kConsumers * kStages * kStageBytes;
 constexpr int kMaxSplits = 32;                    // CTAs per output tile, at most
-constexpr int kMinStagesPerCta = 2;               // K rows per CTA, at least 2 x 32
+constexpr int kMinStagesPerCta = 1;               // K rows per CTA, at least one stage
 // Weight stages per warp that are prefetched into L2 before the dependency wait.
 constexpr int kL2PrefetchStages = 2;
 
@@ -84,6 +85,7 @@ struct DecGeo {
 struct TmaGemvArgs {
   const __half* x;
   int64_t ldx;
+  const int32_t* qw;
   const int32_t* qz;
   const __half* scales;
   __half* out;
@@ -122,6 +124,20 @@ __device__ __forceinline__ uint32_t lds_u16(uint32_t addr) {
   return v;
 }
 
+// 16-byte asynchronous global -> shared copy (no register round trip), awaited with
+// cp_async_wait_all by the issuing thread.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+// One arrival on mbarrier `bar` once all of this thread's earlier cp.async copies have
+// landed (the arrival is not counted in advance: the barrier's count includes it).
+__device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared.b64 [%0];" ::"r"(bar) : "memory");
+}
+
 // Biased unpack: 4 half2 holding (1024 + w) for nibbles at bits 0..3 / 16..19 and
 // (1024 + 16 w) for bits 4..7 / 20..23, of the word and of word >> 8 -- exact values,
 // element pairs (0,1), (2,3), (4,5), (6,7).  No zero subtraction per weight.
@@ -156,7 +172,7 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
   const uint32_t base_raw = sm100::smem_u32(smem_raw);
   const uint32_t sbase = (base_raw + 1023u) & ~1023u;
   unsigned char* sgen = smem_raw + (sbase - base_raw);
-  // layout: ring | stage bars | staging bars (x, zeros + scales) | flags | xs | zs | ss
+  // layout: ring | stage bars | staging bar (x) | flags | xs | zs | ss
   const uint32_t off_full = kRingBytes;
   const uint32_t off_sbar = off_full + kConsumers * kStages * 8;
   const uint32_t off_misc = off_sbar + 16;
@@ -166,7 +182,6 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sgen + off_misc);
   volatile int* last_flag = reinterpret_cast<volatile int*>(sgen + off_misc + 4);
   const uint32_t xbar = sbase + off_sbar;          // activations staged
-  const uint32_t zbar = xbar + 8;                   // zero / scale rows staged
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -200,8 +215,6 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
   const int Kc = nb * 8;
   const int g0 = krow0 / a.gs;
   const int ng = Kc > 0 ? (krow0 + Kc - 1) / a.gs - g0 + 1 : 0;
-  const uint32_t zbytes = (uint32_t)min(32, a.PN - strip * 32) * 4u;      // multiple of 16
-  const uint32_t sbytes = (uint32_t)min(kStripN, a.N - strip * kStripN) * 2u;
   auto full_bar = [&](int w, int s) { return sbase + off_full + (uint32_t)(w * kStages + s) * 8u; };
   auto stage_addr = [&](int w, int s) {
     return sbase + (uint32_t)(w * kStages + s) * kStageBytes;
@@ -213,49 +226,41 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
   if (lane == 0) {
     for (int s2 = 0; s2 < kStages; ++s2) sm100::mbar_init(full_bar(warp, s2), 1);
     if (warp == 0) {
-      sm100::mbar_init(xbar, 1);
-      sm100::mbar_init(zbar, 1);
+      sm100::mbar_init(xbar, kThreads);             // one arrival per thread's x copies
       *abort_flag = 0;
       sm100::prefetch_tmap(&tmW);
     }
     sm100::fence_mbar_init();
   }
-  // ---- before the dependency wait: warm L2 with this CTA's first weight stages and its
-  // zero / scale rows.  These are read-only inputs, and a prefetch only fills L2 -- the
+  __syncthreads();                                   // barriers initialised for every thread
+  // ---- before the dependency wait: warm L2 with this warp's first weight stages, one
+  // 128-byte row segment per lane and prefetch (plain prefetches: they do not occupy the
+  // TMA unit).  The weights are read-only inputs, and a prefetch only fills L2 -- the
   // coherence point -- so it never hands the kernel a stale value; everything that lands
   // in registers or shared memory is read after griddepcontrol.wait.
-  for (int j = lane; j < a.l2pf && j < nst; j += 32)
-    sm100::tma_prefetch_l2_2d(&tmW, strip * 32, (b0 + j * kBlocksPerStage) * 8);
-  if (a.l2pf > 0) {
-    for (int i = tid; i < 2 * ng; i += kThreads) {
-      const int gi = i >> 1;
-      if (i & 1)
-        sm100::bulk_prefetch_l2(a.scales + (int64_t)(g0 + gi) * a.N + strip * kStripN, sbytes);
-      else
-        sm100::bulk_prefetch_l2(a.qz + (int64_t)(g0 + gi) * a.PN + strip * 32, zbytes);
-    }
-  }
+  for (int j = 0; j < a.l2pf && j < nst; ++j)
+#pragma unroll
+    for (int r = lane; r < kRowsPerStage; r += 32)
+      sm100::prefetch_l2(a.qw + (int64_t)((b0 + j * kBlocksPerStage) * 8 + r) * a.PN + strip * 32);
   sm100::grid_dependency_wait();        // no-op unless launched as a programmatic dependent
   sm100::grid_launch_dependents();
 
-  // ---- staging: activations xs[m][k] (Mc rows), then the strip's zero / scale rows, as
-  // bulk copies issued ahead of the weight stages so that they are not queued behind
-  // them.  The main loop needs only the activations to start; for M <= 4 the zero /
-  // scale rows are first read at the end of the first group segment.
-  if (tid == 0) {
-    sm100::mbar_arrive_expect_tx(xbar, (uint32_t)Mc * (uint32_t)Kc * 2u);
-    for (int m = 0; m < Mc; ++m)
-      sm100::bulk_load(sbase + off_xs + (uint32_t)(m * a.xs_stride) * 2u,
-                       a.x + (int64_t)(m0 + m) * a.ldx + krow0, (uint32_t)Kc * 2u, xbar);
-    sm100::mbar_arrive_expect_tx(zbar, (uint32_t)ng * (zbytes + sbytes));
-    for (int gi = 0; gi < ng; ++gi) {
-      sm100::bulk_load(sbase + off_zs + (uint32_t)gi * 128u,
-                       a.qz + (int64_t)(g0 + gi) * a.PN + strip * 32, zbytes, zbar);
-      sm100::bulk_load(sbase + off_ss + (uint32_t)gi * (kStripN * 2u),
-                       a.scales + (int64_t)(g0 + gi) * a.N + strip * kStripN, sbytes, zbar);
+  // ---- staging.  Activations xs[m][k] (Mc rows): 16-byte cp.async copies spread over
+  // all threads, each thread's copies completing as one arrival on xbar.  Weight stages:
+  // every warp its first kStages (lane 0).  Zero / scale rows: every warp those of the
+  // groups its own K range touches, with cp.async, awaited at first use (M <= 4: the end
+  // of the first group segment); a group shared by two warps is copied by both (same
+  // bytes).  Only the weight stages go through the TMA unit, which issues many small
+  // copies slowly.
+  {
+    const int vecs = Kc / 8;                         // 16-byte vectors per token row
+    for (int i = tid; i < Mc * vecs; i += kThreads) {
+      const int m = i / vecs, v = i - m * vecs;
+      cp_async16(sbase + off_xs + (uint32_t)(m * a.xs_stride + v * 8) * 2u,
+                 a.x + (int64_t)(m0 + m) * a.ldx + krow0 + v * 8);
     }
+    cp_async_arrive_noinc(xbar);
   }
-  __syncwarp();
   if (lane == 0) {
     for (int j = 0; j < kStages && j < nst; ++j) {
       sm100::mbar_arrive_expect_tx(full_bar(warp, j), kStageBytes);
@@ -263,10 +268,31 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
                          (b0 + j * kBlocksPerStage) * 8);
     }
   }
-  __syncthreads();                                   // staging barriers initialised for all
+  if (b1 > b0) {
+    const int wg0 = b0 * 8 / a.gs - g0;              // this warp's first group row
+    const int wgn = (b1 * 8 - 1) / a.gs - g0 - wg0 + 1;
+    for (int i = lane; i < wgn * 40; i += 32) {
+      const int gi = wg0 + i / 40, v = i % 40;      // 8 vectors of zeros, 32 of scales
+      if (v < 8) {
+        const int wc = strip * 32 + v * 4;
+        if (wc < a.PN)
+          cp_async16(sbase + off_zs + (uint32_t)(gi * 128 + v * 16),
+                     a.qz + (int64_t)(g0 + gi) * a.PN + wc);
+      } else {
+        const int n = strip * kStripN + (v - 8) * 8;
+        if (n < a.N)
+          cp_async16(sbase + off_ss + (uint32_t)(gi * kStripN * 2 + (v - 8) * 16),
+                     a.scales + (int64_t)(g0 + gi) * a.N + n);
+      }
+    }
+  }
   bool ok = sm100::mbar_wait_bounded(xbar, 0, a.status);
-  bool zs_ready = false;                             // zbar waited by this thread
-  if (!BIAS && ok) ok = zs_ready = sm100::mbar_wait_bounded(zbar, 0, a.status);
+  bool zs_ready = false;                             // this warp's zero / scale rows landed
+  if (!BIAS) {
+    cp_async_wait_all();
+    __syncwarp();
+    zs_ready = true;
+  }
 
   const int chunk = (g >> 1) | ((g & 1) << 2);       // conflict-free word chunk
   float acc[TOKSETS][8][4];
@@ -375,11 +401,8 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
       if constexpr (BIAS) {
         // close the group segment [kb, kend): remove the zero term, apply the scale
         if (!zs_ready) {
-          if (!sm100::mbar_wait_bounded(zbar, 0, a.status)) {
-            *abort_flag = 1;
-            ok = false;
-            break;
-          }
+          cp_async_wait_all();
+          __syncwarp();
           zs_ready = true;
         }
         float part = 0.f;
@@ -428,16 +451,12 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
     }
   }
   if (!ok && lane == 0) {
-    // a copy never arrived: wait (bounded) for this warp's copies still in flight, and
-    // for the staging copies
+    // a copy never arrived: wait (bounded) for this warp's copies still in flight
     for (int jj = j; jj < nst && jj < j + kStages; ++jj)
       sm100::mbar_wait_bounded(full_bar(warp, jj % kStages), (jj / kStages) & 1, nullptr,
                                50000000ull);
-    if (warp == 0) {
-      sm100::mbar_wait_bounded(xbar, 0, nullptr, 50000000ull);
-      sm100::mbar_wait_bounded(zbar, 0, nullptr, 50000000ull);
-    }
   }
+  cp_async_wait_all();                               // no copy into this CTA outlives it
   __syncwarp();
 
   // ---- CTA reduction: each warp parks its partial in its own (now idle) ring, one
@@ -472,10 +491,14 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
   }
   if (nsplit == 1) return;                             // uniform over the CTA
 
-  // ---- split-K: ticket, then the last CTA of the tile sums the slots in order --------
-  __threadfence();                                     // this thread's slot stores first
+  // ---- split-K: after the barrier, one thread publishes the CTA's slot stores (a
+  // gpu-scope fence is cumulative over the stores the barrier ordered before it) and
+  // takes a ticket; the last CTA of the tile sums the slots in slot order --------------
   __syncthreads();
-  if (tid == 0) *last_flag = (atomicAdd(a.cnt + tile, 1) == nsplit - 1) ? 1 : 0;
+  if (tid == 0) {
+    __threadfence();
+    *last_flag = (atomicAdd(a.cnt + tile, 1) == nsplit - 1) ? 1 : 0;
+  }
   __syncthreads();
   if (!*last_flag) return;
   __threadfence();
@@ -630,6 +653,7 @@ cudaError_t launch_gemv_tma(const GemvTmaPlan& p, const void* x, int64_t ldx,
   TmaGemvArgs a;
   a.x = static_cast<const __half*>(x);
   a.ldx = ldx;
+  a.qw = qweight;
   a.qz = qzeros;
   a.scales = static_cast<const __half*>(scales);
   a.out = static_cast<__half*>(out);

@@ -71,24 +71,9 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
       : "memory");
 }
-// L2 prefetch of a tile (no shared-memory write, no completion): always safe to issue
-// before the grid dependency is resolved, because L2 is coherent with later writes.
-__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int c0, int c1) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];"
-               ::"l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1) : "memory");
-}
-// Contiguous global -> shared copy of `bytes` (both addresses 16-byte aligned, size a
-// multiple of 16) that completes on mbarrier `bar` as transaction bytes.
-__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
-                                          uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-      ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
-      : "memory");
-}
-// L2 prefetch of `bytes` contiguous bytes (address 16-byte aligned, size a multiple of 16).
-__device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+// L2 prefetch of the cache line holding p (a hint; no completion, no shared memory).
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 // Programmatic dependent launch: wait until the preceding grid in the stream has
 // completed and its writes are visible; allow the next grid to start launching.
