@@ -51,6 +51,14 @@ SWEEP = {"q_o": (HIDDEN, HIDDEN), "k_v": (HIDDEN, 512), "qkv": (HIDDEN, 4608),
          "gate_up": (HIDDEN, 2 * INTER), "down": (INTER, HIDDEN)}
 
 
+# DRAM bytes (read + write) of one cold-cache launch of the decode kernel at M=1 on each
+# stack shape, from `ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum` (summary and
+# command in profiles/gemv_tma_decode_traffic.md).  Per launch of the stack this averages
+# to within 1 % of the algorithmic bytes: no re-reads.
+NCU_TRAFFIC_M1 = {"qkv": 8628736, "o": 6721536, "gate_up": 70596608 + 478976,
+                  "down": 35353600 + 7424}
+
+
 def alg_bytes(M, K, N, gs=GS):
     """Algorithmic bytes of one call: packed weights + zeros + scales + x + out."""
     return K * N // 2 + (K // gs) * (N // 8) * 4 + (K // gs) * N * 2 + 2 * M * K + 2 * M * N
@@ -66,58 +74,95 @@ def load_peaks():
 
 # --------------------------------------------------------------------------- clocks --
 class ClockSampler:
-    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock and clock-event (throttle) reasons sampled through NVML every 10 ms in a
+    thread while the timed region runs (read-only queries; no GPU setting is changed).
+    The first sample is taken before __enter__ returns, so even a short timed region is
+    covered.  Falls back to nvidia-smi when NVML is unavailable."""
+    PERIOD_S = 0.01
+    # NVML clock-event reason bits
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.rows = []
-        self.proc = None
+    def __init__(self, torch_index: int):
+        self.torch_index = torch_index
+        self.rows = []            # (sm_mhz, max_mhz, reason bits)
+        self.stop = threading.Event()
         self.thread = None
+        self.nvml = None
+        self.handle = None
+
+    def _open(self):
+        import pynvml
+        pynvml.nvmlInit()
+        handle = None
+        try:                                   # match the CUDA device by PCI bus id
+            import torch
+            pr = torch.cuda.get_device_properties(self.torch_index)
+            bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+            handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            handle = pynvml.nvmlDeviceGetHandleByIndex(self.torch_index)
+        return pynvml, handle
+
+    def _sample(self):
+        nv, h = self.nvml, self.handle
+        sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        get = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        self.rows.append((float(sm), float(mx), int(get(h))))
+
+    def _loop(self):
+        while not self.stop.wait(self.PERIOD_S):
+            try:
+                self._sample()
+            except Exception:
+                return
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.nvml, self.handle = self._open()
+            self._sample()
+            self.thread = threading.Thread(target=self._loop, daemon=True)
             self.thread.start()
-        except (OSError, FileNotFoundError):
-            self.proc = None
+        except Exception:
+            self.nvml = None
+            self._smi_once()
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
-                self.rows.append(parts)
+    def _smi_once(self):
+        try:
+            out = subprocess.run(
+                ["nvidia-smi", f"--id={self.torch_index}", "--query-gpu=clocks.sm,clocks.max.sm",
+                 "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=10)
+            sm, mx = (float(v) for v in out.stdout.strip().split(",")[:2])
+            self.rows.append((sm, mx, 0))
+        except Exception:
+            pass
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        if self.thread is not None:
+            self.stop.set()
             self.thread.join(timeout=5)
+            try:
+                self._sample()                 # one more, right after the region
+            except Exception:
+                pass
+        elif self.nvml is None:
+            self._smi_once()
 
     def summary(self):
         if not self.rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = set()
-        for r in self.rows:
-            for i, nm in enumerate(names):
-                if r[5 + i].lower() == "active":
+        for _, _, bits in self.rows:
+            for b, nm in self.REASONS.items():
+                if bits & b:
                     reasons.add(nm)
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(self.rows)}
+        return {"sm_mhz": statistics.median(r[0] for r in self.rows),
+                "sm_max_mhz": max(r[1] for r in self.rows),
+                "reasons": sorted(reasons), "samples": len(self.rows),
+                "source": "nvml" if self.nvml is not None else "nvidia-smi"}
 
 
 # ------------------------------------------------------------------------ helpers ----
@@ -274,8 +319,14 @@ def run_ours(args):
                        "parallelism": f"tp{world}" if world > 1 else "single"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak,
                          "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
-                         "peak_source": peak_src, "traffic": None,
-                         "kernel": "awq::gemv_kernel (decode, mma.sync split-K)"},
+                         "peak_source": peak_src,
+                         "traffic": (round(sum(NCU_TRAFFIC_M1.values()) / len(NCU_TRAFFIC_M1))
+                                     if world == 1 else None),
+                         "traffic_note": "bytes per launch averaged over the 4 stack shapes, "
+                                         "ncu dram__bytes_read.sum + dram__bytes_write.sum",
+                         "alg_bytes_per_launch": round(local_bytes / len(calls)),
+                         "kernel": "awq::gemv_tma_kernel<1> (decode: TMA-streamed mma.sync, "
+                                   "one CTA per SM, deterministic split-K)"},
             "gpu_launches": args.steps * len(calls),
         }
         result["clocks"] = clk.summary()
@@ -492,7 +543,7 @@ def main():
                     help="profile one kernel: decode:<shape>:<M>, prefill:<shape>:<M>, dequant:<shape>")
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)

@@ -585,8 +585,9 @@ cudaError_t launch_t(const CUtensorMap& tm, const TmaGemvArgs& a, int grid, size
 }  // namespace
 
 // One CTA per SM when the tiles allow it (each CTA gets at least kMinStagesPerCta
-// stages, a tile at most kMaxSplits CTAs); one more CTA per tile at a time while the
-// largest K range's staged activations and zero / scale rows do not fit in shared memory.
+// stages, a tile at most kMaxSplits CTAs and at most 64 / tokens); one more CTA per tile
+// at a time while the largest K range's staged activations and zero / scale rows do not
+// fit in shared memory.
 bool plan_gemv_tma(int64_t M, int64_t N, int64_t K, int64_t gs, int num_sms, GemvTmaPlan* p) {
   if (M <= 0 || M > 16 || N <= 0 || N % 32 || gs % kRowsPerStage || K <= 0 || K % gs ||
       num_sms <= 0)
@@ -598,8 +599,11 @@ bool plan_gemv_tma(int64_t M, int64_t N, int64_t K, int64_t gs, int num_sms, Gem
   const int64_t nstage = K / kRowsPerStage;                   // stages per tile
   int64_t grid0 = tiles;
   if (tiles < num_sms) {
+    // the last CTA of a tile reads (tokens x CTAs per tile) partial rows: keep it short
+    const int64_t mc = M < MP ? M : MP;
     int64_t maxc = nstage / kMinStagesPerCta;
     if (maxc > kMaxSplits) maxc = kMaxSplits;
+    if (maxc > 64 / mc) maxc = 64 / mc;
     if (maxc < 1) maxc = 1;
     grid0 = tiles * maxc < num_sms ? tiles * maxc : num_sms;
   }

@@ -66,7 +66,7 @@ cudaError_t launch_gemv_tma(const GemvTmaPlan& plan, const void* x, int64_t ldx,
                             const int32_t* qweight, const int32_t* qzeros, const void* scales,
                             void* out, int64_t ldo, int M, int N, int K, int group_size,
                             void* workspace, int* dev_status, cudaStream_t stream);
-constexpr size_t kGemvTmaMaxSmem = 200 * 1024;
+constexpr size_t kGemvTmaMaxSmem = 227 * 1024;   // sm_100's opt-in per-block maximum
 
 // ---- prefill GEMM on tcgen05 / TMEM (awq_gemm_tc.cu) ----------------------------------
 // Returns true when the tcgen05 kernel can run this shape (alignment / TMA rules).
