@@ -32,14 +32,14 @@
 //   groups; the loop starts on the activations alone.
 // Math: dequantized pairs feed mma.sync.m16n8k16 (fp16 x fp16 -> fp32) with the
 //   activations spread over the (token, pair-slot) B columns.  For M <= 4 the MMA takes
-//   the exact biased values 1024 + w / 1024 + 16 w and the zero term
-//   (1024 + z) * sum(x) / (1024 + 16 z) * sum(x) is removed per group in fp32 before the
-//   fp32 scale (scale / 16) is applied; for M > 4 W is rounded to fp16 first exactly as
-//   the reference does.
+//   the exact biased values 1024 + w / 1024 + 16 w; each group segment's fp32 accumulator
+//   starts at -(1024 + z) * sum(x) (resp. -(1024 + 16 z) * sum(x)), computed while the
+//   segment's stages are in flight, and the fp32 scale (scale / 16) is applied when the
+//   segment closes; for M > 4 W is rounded to fp16 first exactly as the reference does.
 // Split-K: each CTA sums its 8 warps' partials in shared memory (fixed order).  A tile
 //   with one CTA writes fp16 directly.  Otherwise each CTA writes an fp32 partial into
-//   its own workspace slot, and the last CTA of the tile to take a ticket (an atomic
-//   counter, which that CTA resets) sums the tile's slots in slot order --
+//   its own workspace slot, and the last CTA of the tile to take a ticket (an acq_rel
+//   atomic counter, which that CTA resets) sums the tile's slots in slot order --
 //   deterministic -- and writes fp16.
 // Every mbarrier wait is bounded (status word + early exit, after a bounded drain of
 // the copies still in flight).
@@ -136,6 +136,13 @@ __device__ __forceinline__ void cp_async_wait_all() {
 // landed (the arrival is not counted in advance: the barrier's count includes it).
 __device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// Atomic add at gpu scope with acquire-release ordering; returns the old value.
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
 }
 
 // Biased unpack: 4 half2 holding (1024 + w) for nibbles at bits 0..3 / 16..19 and
@@ -321,6 +328,7 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
     }
     uint32_t zcst[4][4], scl[4][4];
     float pacc[BIAS ? 8 : 1][4];
+    float gsc[BIAS ? 8 : 1][4];                         // M <= 4: the segment's scales
     for (int kb = b0 * 8; kb < b1 * 8 && ok;) {
       const int grp = kb / a.gs;
       const int kend = min(b1 * 8, (grp + 1) * a.gs);
@@ -336,10 +344,61 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
           scl[c][0] = s4.x; scl[c][1] = s4.y; scl[c][2] = s4.z; scl[c][3] = s4.w;
         }
       } else {
+        // M <= 4: everything of the segment's zero / scale correction that does not need
+        // the MMA results is done here, while the segment's stages are still in flight:
+        // pacc starts at -(1024 + z) * sum(x) (resp. -(1024 + 16 z) * sum(x)), so after
+        // the MMAs add sum((1024 + w) x) it holds sum((w - z) x) (resp. 16x that); the
+        // scale (resp. scale / 16) is applied when the segment closes.
+        if (!zs_ready) {
+          cp_async_wait_all();
+          __syncwarp();
+          zs_ready = true;
+        }
+        float part = 0.f;                               // sum(x[token t]) over the segment
+        if (t < Mc) {
+          const int u0 = (kb - krow0) >> 3, u1 = (kend - krow0) >> 3;
+          const uint32_t xt = sbase + off_xs + (uint32_t)(t * a.xs_stride) * 2u;
+          for (int u = u0 + g; u < u1; u += 8) {
+            const uint4 v = lds128(xt + (uint32_t)u * 16u);
+            const uint32_t hv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-        for (int q = 0; q < 8; ++q)
+            for (int k = 0; k < 4; ++k) {
+              const float2 f = __half22float2(u32_as_h2(hv[k]));
+              part += f.x + f.y;
+            }
+          }
+        }
+        part += __shfl_xor_sync(0xffffffffu, part, 4);
+        part += __shfl_xor_sync(0xffffffffu, part, 8);
+        part += __shfl_xor_sync(0xffffffffu, part, 16);
+        const uint4 z4 = lds128(sbase + off_zs + (uint32_t)(gl * 128 + chunk * 16));
+        const uint32_t zw[4] = {z4.x, z4.y, z4.z, z4.w};
 #pragma unroll
-          for (int i = 0; i < 4; ++i) pacc[q][i] = 0.f;
+        for (int c = 0; c < 4; ++c) {
+          const uint4 s4 = lds128(sbase + off_ss + (uint32_t)(gl * kStripN * 2 + (chunk * 4 + c) * 16));
+          const uint32_t sv[4] = {s4.x, s4.y, s4.z, s4.w};
+          const uint32_t z8 = zw[c] >> 8;
+          const uint32_t zb[4] = {lop3_and_or(zw[c], kLoMask, kMagic),   // 1024 + z
+                                  lop3_and_or(zw[c], kHiMask, kMagic),   // 1024 + 16 z
+                                  lop3_and_or(z8, kLoMask, kMagic),
+                                  lop3_and_or(z8, kHiMask, kMagic)};
+#pragma unroll
+          for (int jj = 0; jj < 2; ++jj) {
+            const int q = 2 * c + jj;
+            const float2 zl = __half22float2(u32_as_h2(zb[2 * jj]));
+            const float2 zh = __half22float2(u32_as_h2(zb[2 * jj + 1]));
+            const float2 sl = __half22float2(u32_as_h2(sv[2 * jj]));
+            const float2 sh = __half22float2(u32_as_h2(sv[2 * jj + 1]));
+            pacc[q][0] = -zl.x * part;
+            pacc[q][1] = -zl.y * part;
+            pacc[q][2] = -zh.x * part;
+            pacc[q][3] = -zh.y * part;
+            gsc[q][0] = sl.x;
+            gsc[q][1] = sl.y;
+            gsc[q][2] = sh.x * 0.0625f;
+            gsc[q][3] = sh.y * 0.0625f;
+          }
+        }
       }
       const int nseg = (kend - kb) / kRowsPerStage;
       for (int i = 0; i < nseg; ++i, ++j) {
@@ -399,53 +458,12 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
         }
       }
       if constexpr (BIAS) {
-        // close the group segment [kb, kend): remove the zero term, apply the scale
-        if (!zs_ready) {
-          cp_async_wait_all();
-          __syncwarp();
-          zs_ready = true;
-        }
-        float part = 0.f;
-        if (t < Mc) {
-          const int u0 = (kb - krow0) >> 3, u1 = (kend - krow0) >> 3;
-          const uint32_t xt = sbase + off_xs + (uint32_t)(t * a.xs_stride) * 2u;
-          for (int u = u0 + g; u < u1; u += 8) {
-            const uint4 v = lds128(xt + (uint32_t)u * 16u);
-            const uint32_t hv[4] = {v.x, v.y, v.z, v.w};
+        // close the group segment: apply the group's scale (the zero term is already in
+        // pacc, seeded at the segment's start)
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const float2 f = __half22float2(u32_as_h2(hv[k]));
-              part += f.x + f.y;
-            }
-          }
-        }
-        part += __shfl_xor_sync(0xffffffffu, part, 4);
-        part += __shfl_xor_sync(0xffffffffu, part, 8);
-        part += __shfl_xor_sync(0xffffffffu, part, 16);   // sum(x[token t]) over the segment
-        const uint4 z4 = lds128(sbase + off_zs + (uint32_t)(gl * 128 + chunk * 16));
-        const uint32_t zw[4] = {z4.x, z4.y, z4.z, z4.w};
+        for (int q = 0; q < 8; ++q)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const uint4 s4 = lds128(sbase + off_ss + (uint32_t)(gl * kStripN * 2 + (chunk * 4 + c) * 16));
-          const uint32_t sv[4] = {s4.x, s4.y, s4.z, s4.w};
-          const uint32_t z8 = zw[c] >> 8;
-          const uint32_t zb[4] = {lop3_and_or(zw[c], kLoMask, kMagic),   // 1024 + z
-                                  lop3_and_or(zw[c], kHiMask, kMagic),   // 1024 + 16 z
-                                  lop3_and_or(z8, kLoMask, kMagic),
-                                  lop3_and_or(z8, kHiMask, kMagic)};
-#pragma unroll
-          for (int jj = 0; jj < 2; ++jj) {
-            const int q = 2 * c + jj;
-            const float2 zl = __half22float2(u32_as_h2(zb[2 * jj]));
-            const float2 zh = __half22float2(u32_as_h2(zb[2 * jj + 1]));
-            const float2 sl = __half22float2(u32_as_h2(sv[2 * jj]));
-            const float2 sh = __half22float2(u32_as_h2(sv[2 * jj + 1]));
-            acc[0][q][0] = fmaf(sl.x, fmaf(-zl.x, part, pacc[q][0]), acc[0][q][0]);
-            acc[0][q][1] = fmaf(sl.y, fmaf(-zl.y, part, pacc[q][1]), acc[0][q][1]);
-            acc[0][q][2] = fmaf(sh.x * 0.0625f, fmaf(-zh.x, part, pacc[q][2]), acc[0][q][2]);
-            acc[0][q][3] = fmaf(sh.y * 0.0625f, fmaf(-zh.y, part, pacc[q][3]), acc[0][q][3]);
-          }
-        }
+          for (int i = 0; i < 4; ++i) acc[0][q][i] = fmaf(gsc[q][i], pacc[q][i], acc[0][q][i]);
       }
       kb = kend;
     }
@@ -491,17 +509,14 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
   }
   if (nsplit == 1) return;                             // uniform over the CTA
 
-  // ---- split-K: after the barrier, one thread publishes the CTA's slot stores (a
-  // gpu-scope fence is cumulative over the stores the barrier ordered before it) and
-  // takes a ticket; the last CTA of the tile sums the slots in slot order --------------
+  // ---- split-K: after the barrier, one thread takes a ticket with an acq_rel atomic
+  // (gpu scope): its release is cumulative over the slot stores the barrier ordered
+  // before it, its acquire (passed on by the next barrier) makes the other CTAs' slots
+  // visible to the last CTA, which sums the tile's slots in slot order ---------------
   __syncthreads();
-  if (tid == 0) {
-    __threadfence();
-    *last_flag = (atomicAdd(a.cnt + tile, 1) == nsplit - 1) ? 1 : 0;
-  }
+  if (tid == 0) *last_flag = (atom_add_acq_rel_gpu(a.cnt + tile, 1) == nsplit - 1) ? 1 : 0;
   __syncthreads();
   if (!*last_flag) return;
-  __threadfence();
   for (int idx = tid; idx < Mc * kStripN; idx += kThreads) {
     const int m = idx / kStripN, nl = idx - m * kStripN;
     const int n = nbase + nl;
