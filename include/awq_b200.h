@@ -117,10 +117,58 @@ AWQ_API int awq_tc_supported(const void* x, int64_t ldx, const int32_t* qweight,
 /*
  * Synchronizes `stream`, then reads and clears the current device's kernel status
  * word.  Returns AWQ_OK, or AWQ_ERR_DEVICE with the status bits in *status_out
- * (1 = a bounded barrier wait timed out, 2 = a kernel rejected its parameters).
+ * (1 = a bounded barrier wait timed out, 2 = a kernel rejected its parameters,
+ * 4 = a fused all-reduce gave up waiting for other ranks).
  * No counterpart in the reference.
  */
 AWQ_API int awq_device_status(void* stream, int* status_out);
+
+/*
+ * ---- Tensor parallelism: the row-parallel product fused with its all-reduce -------------
+ * For the row-parallel linears of a tensor-parallel model (o_proj and down_proj split
+ * along K over `world` GPUs of one box, one process per GPU), awq_gemm_f16_allreduce
+ * computes this rank's partial product and sums it over all ranks in the same kernel:
+ * the last CTA of each output tile stores its fp32 tile into every rank's receive buffer
+ * over NVLink (CUDA IPC peer mappings, plain stores), adds 1 to every rank's counter for
+ * the tile, waits (bounded) until all ranks' tiles are in its own buffer and sums them in
+ * rank order, so every rank writes the same fp16 bits.  It replaces the awq_gemm_f16 +
+ * NCCL all-reduce pair of a row-parallel layer (the reference has no tensor
+ * parallelism: inference/engine.py:15).
+ *
+ * Set-up, once per rank -- the only entry points that allocate device memory and
+ * synchronize the device:
+ *   awq_tp_comm_create(world, rank, max_n, handle, &comm)  this rank's buffer + its handle
+ *   gather the world handles in rank order (e.g. torch.distributed.all_gather_object)
+ *   awq_tp_comm_open(comm, handles)                         maps the other ranks' buffers
+ * Every rank must then issue the same sequence of awq_gemm_f16_allreduce calls, in one
+ * stream per communicator (CUDA-graph capture is fine).  awq_tp_comm_destroy after the
+ * device has finished all calls.  max_n bounds N of the calls (multiple of 8).
+ */
+typedef struct awq_tp_comm awq_tp_comm;
+#define AWQ_IPC_HANDLE_BYTES 64
+#define AWQ_MAX_WORLD 8
+
+AWQ_API int awq_tp_comm_create(int world, int rank, int64_t max_n, void* handle_out,
+                               awq_tp_comm** comm_out);
+AWQ_API int awq_tp_comm_open(awq_tp_comm* comm, const void* handles);
+/* Longest wait for the other ranks' tiles, in ns (default 2 s); then status bit 4. */
+AWQ_API int awq_tp_comm_set_timeout(awq_tp_comm* comm, uint64_t timeout_ns);
+AWQ_API int awq_tp_comm_destroy(awq_tp_comm* comm);
+
+/* 1 if awq_gemm_f16_allreduce can run this call (the decode kernel with one CTA per SM
+ * in a single wave: N % 32 == 0, group_size % 64 == 0, 16-byte aligned qweight and x,
+ * ldx % 8 == 0, N <= max_n), else 0.  Otherwise use awq_gemm_f16 + an all-reduce. */
+AWQ_API int awq_allreduce_supported(const awq_tp_comm* comm, const void* x, int64_t ldx,
+                                    const int32_t* qweight, int64_t M, int64_t N, int64_t K,
+                                    int64_t group_size);
+
+/* out[M, N] = sum over ranks of (this rank's x[M, K_r] @ W_r), written on every rank.
+ * Workspace as for awq_gemm_f16 (awq_gemm_workspace_bytes). */
+AWQ_API int awq_gemm_f16_allreduce(awq_tp_comm* comm, const void* x, int64_t ldx,
+                                   const int32_t* qweight, const int32_t* qzeros,
+                                   const void* scales, void* out, int64_t ldo, int64_t M,
+                                   int64_t N, int64_t K, int64_t group_size, void* workspace,
+                                   size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

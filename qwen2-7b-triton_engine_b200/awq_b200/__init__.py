@@ -22,7 +22,7 @@ from . import _lib
 from ._lib import (AWQ_PATH_AUTO, AWQ_PATH_DECODE, AWQ_PATH_TC, AwqError,  # noqa: F401
                    LIB_PATH)
 
-__all__ = ["dequant", "gemm", "device_status", "workspace_for", "AwqError",
+__all__ = ["dequant", "gemm", "gemm_allreduce", "TPComm", "device_status", "workspace_for", "AwqError",
            "AWQ_PATH_AUTO", "AWQ_PATH_DECODE", "AWQ_PATH_TC", "LIB_PATH"]
 
 _ws_lock = threading.Lock()
@@ -168,6 +168,102 @@ def gemm(x2d: torch.Tensor, qweight: torch.Tensor, qzeros: torch.Tensor, scales:
             scales.data_ptr(), out.data_ptr(), out.stride(0), M, N, K, int(group_size),
             ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
             _stream_handle(dev), int(path)))
+    return out
+
+
+class TPComm:
+    """This rank's communicator for the fused row-parallel all-reduce
+    (``awq_tp_comm_*`` / ``awq_gemm_f16_allreduce`` in include/awq_b200.h): a receive
+    buffer on this rank's GPU that every other rank maps through CUDA IPC and writes its
+    tile results into over NVLink.
+
+    ``TPComm(world, rank, max_n)`` allocates the buffer on the current device and exposes
+    ``handle`` (bytes); ``open(handles)`` takes every rank's handle in rank order.
+    ``TPComm.from_group(max_n, group)`` does both with ``torch.distributed``.  All ranks
+    must then issue the same sequence of ``gemm_allreduce`` calls, one stream per
+    communicator.  ``close()`` after the device has finished those calls."""
+
+    def __init__(self, world: int, rank: int, max_n: int, device=None):
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None \
+            else torch.device(device)
+        self.world, self.rank, self.max_n = int(world), int(rank), int(max_n)
+        lib = _lib.load()
+        h = ctypes.create_string_buffer(_lib.AWQ_IPC_HANDLE_BYTES)
+        ptr = ctypes.c_void_p()
+        with _DeviceGuard(self.device):
+            _lib.check(lib.awq_tp_comm_create(self.world, self.rank, self.max_n, h,
+                                              ctypes.byref(ptr)))
+        self._ptr = ptr
+        self.handle = h.raw
+        self.opened = False
+
+    def open(self, handles) -> None:
+        if len(handles) != self.world or any(len(h) != _lib.AWQ_IPC_HANDLE_BYTES for h in handles):
+            raise ValueError(f"need {self.world} handles of {_lib.AWQ_IPC_HANDLE_BYTES} bytes")
+        buf = ctypes.create_string_buffer(b"".join(handles), len(handles) * _lib.AWQ_IPC_HANDLE_BYTES)
+        with _DeviceGuard(self.device):
+            _lib.check(_lib.load().awq_tp_comm_open(self._ptr, buf))
+        self.opened = True
+
+    @classmethod
+    def from_group(cls, max_n: int, group=None, device=None) -> "TPComm":
+        import torch.distributed as dist
+        comm = cls(dist.get_world_size(group), dist.get_rank(group), max_n, device)
+        handles = [None] * comm.world
+        dist.all_gather_object(handles, comm.handle, group=group)
+        comm.open(handles)
+        dist.barrier(group=group)
+        return comm
+
+    def set_timeout(self, seconds: float) -> None:
+        _lib.check(_lib.load().awq_tp_comm_set_timeout(self._ptr, max(1, int(seconds * 1e9))))
+
+    def supported(self, x2d: torch.Tensor, qweight: torch.Tensor, N: int,
+                  group_size: int = 128) -> bool:
+        if not self.opened:
+            return False
+        with _DeviceGuard(self.device):
+            return bool(_lib.load().awq_allreduce_supported(
+                self._ptr, x2d.data_ptr(), x2d.stride(0), qweight.data_ptr(), x2d.shape[0], N,
+                qweight.shape[0], int(group_size)))
+
+    def close(self) -> None:
+        if self._ptr is not None:
+            with _DeviceGuard(self.device):
+                _lib.check(_lib.load().awq_tp_comm_destroy(self._ptr))
+            self._ptr = None
+
+
+def gemm_allreduce(x2d: torch.Tensor, qweight: torch.Tensor, qzeros: torch.Tensor,
+                   scales: torch.Tensor, group_size: int, comm: TPComm,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    """Row-parallel product summed over the tensor-parallel ranks in one kernel: every
+    rank gets fp16 [M, N] = sum over ranks of x2d_r @ W_r (bit-identical on all ranks).
+    Raises AwqError(AWQ_ERR_UNSUPPORTED) when ``comm.supported`` is false."""
+    K, N = check_weights(qweight, qzeros, scales, group_size)
+    _require_cuda(x2d, "x")
+    if x2d.dtype != torch.float16 or x2d.dim() != 2 or x2d.shape[1] != K:
+        raise ValueError(f"x must be float16 [M, K={K}], got {x2d.dtype} {tuple(x2d.shape)}")
+    M = x2d.shape[0]
+    dev = x2d.device
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float16, device=dev)
+    if M == 0:
+        return out
+    qweight, qzeros, scales = _dense16(qweight), _dense16(qzeros), _dense16(scales)
+    if x2d.stride(1) != 1 or x2d.data_ptr() % 16 or (x2d.stride(0) * 2) % 16:
+        x2d = x2d.contiguous()
+        if x2d.data_ptr() % 16:
+            x2d = x2d.clone()
+    lib = _lib.load()
+    with _DeviceGuard(dev):
+        need = lib.awq_gemm_workspace_bytes(M, N, K, int(group_size))
+        ws = workspace_for(dev, need) if need else None
+        _lib.check(lib.awq_gemm_f16_allreduce(
+            comm._ptr, x2d.data_ptr(), x2d.stride(0), qweight.data_ptr(), qzeros.data_ptr(),
+            scales.data_ptr(), out.data_ptr(), out.stride(0), M, N, K, int(group_size),
+            ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
+            _stream_handle(dev)))
     return out
 
 

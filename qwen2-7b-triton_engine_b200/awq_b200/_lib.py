@@ -41,7 +41,21 @@ SIGNATURES = {
     "awq_gemm_f16_noalloc": ([_P, _I64, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P], _INT),
     "awq_tc_supported": ([_P, _I64, _P, _P, _P, _I64, _I64, _I64, _I64], _INT),
     "awq_device_status": ([_P, ctypes.POINTER(ctypes.c_int)], _INT),
+    "awq_tp_comm_create": ([_INT, _INT, _I64, _P, ctypes.POINTER(_P)], _INT),
+    "awq_tp_comm_open": ([_P, _P], _INT),
+    "awq_tp_comm_set_timeout": ([_P, ctypes.c_uint64], _INT),
+    "awq_tp_comm_destroy": ([_P], _INT),
+    "awq_allreduce_supported": ([_P, _P, _I64, _P, _I64, _I64, _I64, _I64], _INT),
+    "awq_gemm_f16_allreduce": ([_P, _P, _I64, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P,
+                                _SZ, _P], _INT),
 }
+
+AWQ_IPC_HANDLE_BYTES = 64
+AWQ_MAX_WORLD = 8
+# bits of the device status word (awq_device_status)
+STATUS_BARRIER_TIMEOUT = 1
+STATUS_SHAPE = 2
+STATUS_PEER_TIMEOUT = 4
 
 _lib = None
 

@@ -122,21 +122,47 @@ class ColumnParallelAWQ:
 
 
 class RowParallelAWQ:
-    """Rank's K-row slice of an AWQ linear; the partial outputs are all-reduced."""
+    """Rank's K-row slice of an AWQ linear; the partial outputs are all-reduced.
+
+    With ``comm`` (an ``awq_b200.TPComm``) a call the fused kernel supports -- decode,
+    M <= 16 per launch -- runs the product and the all-reduce in one kernel
+    (``awq_b200.gemm_allreduce``: peer stores over NVLink, sum in rank order); other
+    calls use the library product and an NCCL all-reduce.  The choice depends on shapes
+    only, so every rank takes the same one."""
 
     def __init__(self, full: AWQWeights, world: int, rank: int, group: Optional[object] = None,
-                 gemm: Optional[GemmFn] = None):
+                 gemm: Optional[GemmFn] = None, comm=None):
         K = full.qweight.shape[0]
         self.k0, self.k1 = row_bounds(K, full.group_size, world, rank)
         qw, qz, s = shard_rows(full.qweight, full.qzeros, full.scales, self.k0, self.k1,
                                full.group_size)
         self.w = AWQWeights(qw, qz, s, full.group_size, full.bias if rank == 0 else None)
+        self.bias = full.bias
         self.group = group
         self.world = world
         self.gemm = gemm or _default_gemm()
+        self.comm = comm
+
+    def _fused(self, x_local: torch.Tensor) -> Optional[torch.Tensor]:
+        import awq_b200
+        if self.comm is None or self.world < 2 or self.k1 <= self.k0:
+            return None
+        x2 = x_local.reshape(-1, x_local.shape[-1])
+        if x2.stride(1) != 1 or x2.data_ptr() % 16 or (x2.stride(0) * 2) % 16:
+            x2 = x2.contiguous().clone()
+        N = self.w.scales.shape[1]
+        if not self.comm.supported(x2, self.w.qweight, N, self.w.group_size):
+            return None
+        out = awq_b200.gemm_allreduce(x2, self.w.qweight, self.w.qzeros, self.w.scales,
+                                      self.w.group_size, self.comm)
+        out = out.view(*x_local.shape[:-1], N)
+        return out + self.bias if self.bias is not None else out
 
     def __call__(self, x_local: torch.Tensor) -> torch.Tensor:
         """x_local holds this rank's K columns [k0, k1) of the activation."""
+        fused = self._fused(x_local)
+        if fused is not None:
+            return fused
         if self.k1 > self.k0:
             out = self.gemm(x_local, self.w.qweight, self.w.qzeros, self.w.scales,
                             self.w.group_size)
@@ -158,7 +184,8 @@ class TensorParallelMLP:
     gate/up columns [lo, hi) are exactly the K rows of down it holds."""
 
     def __init__(self, gate_up: AWQWeights, down: AWQWeights, intermediate: int, world: int,
-                 rank: int, group: Optional[object] = None, gemm: Optional[GemmFn] = None):
+                 rank: int, group: Optional[object] = None, gemm: Optional[GemmFn] = None,
+                 comm=None):
         if down.qweight.shape[0] != intermediate:
             raise ValueError("down must have K == intermediate")
         gs = down.group_size
@@ -169,7 +196,7 @@ class TensorParallelMLP:
         self.gate_up = ColumnParallelAWQ(gate_up, world, rank, parts=[intermediate, intermediate],
                                          gemm=gemm, bounds=bounds)
         self.inter_local = self.gate_up.parts_local[0]
-        self.down = RowParallelAWQ(down, world, rank, group=group, gemm=gemm)
+        self.down = RowParallelAWQ(down, world, rank, group=group, gemm=gemm, comm=comm)
         assert (self.down.k1 - self.down.k0) == self.inter_local
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:

@@ -235,6 +235,69 @@ int awq_gemm_f16(const void* x, int64_t ldx, const int32_t* qweight, const int32
                          workspace_bytes, stream, AWQ_PATH_AUTO);
 }
 
+int awq_allreduce_supported(const awq_tp_comm* comm, const void* x, int64_t ldx,
+                            const int32_t* qweight, int64_t M, int64_t N, int64_t K,
+                            int64_t group_size) {
+  DeviceInfo* d = nullptr;
+  if (!comm || !comm->ready || device_info(&d)) return 0;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev != comm->device) return 0;
+  if (M <= 0 || N <= 0 || N > comm->max_n || group_size <= 0 || K <= 0 || K % group_size) return 0;
+  if (!awq::gemv_tma_supported(qweight, N, ldx, x)) return 0;
+  // every launch must run its CTAs in one wave: a tile's last CTA waits for the other
+  // ranks, and must never hold an SM that a not-yet-started CTA of its own grid needs
+  for (const int64_t mc : {M < 16 ? M : (int64_t)16, M > 16 ? M % 16 : (int64_t)0}) {
+    if (mc == 0) continue;
+    awq::GemvTmaPlan p;
+    if (!awq::plan_gemv_tma(mc, N, K, group_size, d->num_sms, &p) || p.grid > d->num_sms ||
+        p.tiles > comm->max_tiles)
+      return 0;
+  }
+  return 1;
+}
+
+int awq_gemm_f16_allreduce(awq_tp_comm* comm, const void* x, int64_t ldx, const int32_t* qweight,
+                           const int32_t* qzeros, const void* scales, void* out, int64_t ldo,
+                           int64_t M, int64_t N, int64_t K, int64_t group_size, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  int rc = check_weights(qweight, qzeros, scales, K, N, group_size);
+  if (rc) return rc;
+  if (!comm || !comm->ready) return fail(AWQ_ERR_INVALID_ARG, "communicator missing or not opened");
+  if (!x || !out) return fail(AWQ_ERR_INVALID_ARG, "null x or out");
+  if (M <= 0 || M > (int64_t)1 << 30) return fail(AWQ_ERR_INVALID_ARG, "M=%lld out of range", (long long)M);
+  if (ldx < K || ldo < N) return fail(AWQ_ERR_INVALID_ARG, "ldx < K or ldo < N");
+  if ((reinterpret_cast<uintptr_t>(out) & 1)) return fail(AWQ_ERR_INVALID_ARG, "out must be 2-byte aligned");
+  if (!awq_allreduce_supported(comm, x, ldx, qweight, M, N, K, group_size))
+    return fail(AWQ_ERR_UNSUPPORTED, "fused all-reduce cannot run M=%lld N=%lld K=%lld gs=%lld here "
+                "(see awq_allreduce_supported)", (long long)M, (long long)N, (long long)K,
+                (long long)group_size);
+  DeviceInfo* d = nullptr;
+  if ((rc = device_info(&d))) return rc;
+  awq::ArArgs ar;
+  if (!awq::tp_ar_args(comm, &ar)) return fail(AWQ_ERR_INVALID_ARG, "communicator not opened");
+  awq::GemvTmaPlan full = {}, rest = {};
+  const int64_t m_full = M < 16 ? M : 16, m_rest = M > 16 ? M % 16 : 0;
+  awq::plan_gemv_tma(m_full, N, K, group_size, d->num_sms, &full);
+  if (m_rest) awq::plan_gemv_tma(m_rest, N, K, group_size, d->num_sms, &rest);
+  size_t need = full.ws_bytes;
+  if (m_rest > 0 && rest.ws_bytes > need) need = rest.ws_bytes;
+  if (need > 0 && (!workspace || workspace_bytes < need))
+    return fail(AWQ_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  if (need > 0 && !aligned16(workspace))
+    return fail(AWQ_ERR_INVALID_ARG, "workspace must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const char* xb = static_cast<const char*>(x);
+  char* ob = static_cast<char*>(out);
+  for (int64_t m0 = 0; m0 < M; m0 += 16) {
+    const int64_t mc = M - m0 < 16 ? M - m0 : 16;
+    cudaError_t e = awq::launch_gemv_tma(mc == m_full ? full : rest, xb + 2 * m0 * ldx, ldx, qweight,
+                                         qzeros, scales, ob + 2 * m0 * ldo, ldo, (int)mc, (int)N,
+                                         (int)K, (int)group_size, workspace, d->status, st, &ar);
+    if (e != cudaSuccess) return fail_cuda(e, "fused all-reduce kernel launch");
+  }
+  return AWQ_OK;
+}
+
 int awq_device_status(void* stream, int* status_out) {
   DeviceInfo* d = nullptr;
   int rc = device_info(&d);

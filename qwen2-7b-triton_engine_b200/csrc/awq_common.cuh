@@ -30,6 +30,7 @@ enum DeviceError : int {
   kDevErrNone = 0,
   kDevErrBarrierTimeout = 1,   // an mbarrier wait gave up (bounded spin)
   kDevErrShape = 2,            // a kernel saw parameters it cannot handle
+  kDevErrPeerTimeout = 4,      // a wait for other ranks' all-reduce contributions gave up
 };
 
 __device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t mask, uint32_t orv) {

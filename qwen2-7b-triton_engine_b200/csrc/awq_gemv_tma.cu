@@ -100,6 +100,7 @@ struct TmaGemvArgs {
   int ngrp_cta;    // zs / ss rows reserved (quantization groups a CTA's K range touches)
   int l2pf;        // weight stages each warp prefetches into L2 before the dependency wait
   int* status;
+  ArArgs ar;       // fused all-reduce across tensor-parallel ranks (ar.world == 1: none)
 };
 
 __device__ __forceinline__ void mma_16816(float c[4], uint32_t a0, uint32_t a1, uint32_t a2,
@@ -136,6 +137,19 @@ __device__ __forceinline__ void cp_async_wait_all() {
 // landed (the arrival is not counted in advance: the barrier's count includes it).
 __device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// Fused all-reduce: value and flag packed in one aligned 64-bit word (flag in the high
+// half), written with one store -- single-copy atomic, so it arrives whole at the
+// receiver, local or a peer over NVLink -- and polled with one volatile 64-bit load.
+__device__ __forceinline__ void st_pair(unsigned long long* p, float v, uint32_t flag) {
+  const unsigned long long w = ((unsigned long long)flag << 32) | __float_as_uint(v);
+  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ uint2 ld_pair(const unsigned long long* p) {
+  unsigned long long w;
+  asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return make_uint2((uint32_t)w, (uint32_t)(w >> 32));   // {value bits, flag}
 }
 
 // Atomic add at gpu scope with acquire-release ordering; returns the old value.
@@ -493,6 +507,23 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
   __syncthreads();
   const int nbase = strip * kStripN;
   const size_t slot_stride = (size_t)MP * kStripN;
+  // the tile's result leaves through emit(): fp16 to out, or (tensor parallel) fp32 to
+  // this tile's slot on every rank for the fused all-reduce
+  const bool ar = a.ar.world > 1;
+  const uint32_t epoch = ar ? (uint32_t)*reinterpret_cast<volatile int*>(a.ar.state) : 0u;
+  const uint32_t flag = epoch + 1u;
+  const size_t ar_rank_stride = (size_t)a.ar.max_tiles * kArTileFloats;
+  const size_t ar_tile = ((size_t)(epoch & 1u) * a.ar.world * a.ar.max_tiles + tile) * kArTileFloats;
+  auto emit = [&](int idx, int m, int n, float v) {
+    if (!ar) {
+      a.out[(int64_t)(m0 + m) * a.ldo + n] = __float2half_rn(v);
+    } else {
+      const size_t off = ar_tile + (size_t)a.ar.rank * ar_rank_stride + idx;
+#pragma unroll
+      for (int r = 0; r < kMaxWorld; ++r)
+        if (r < a.ar.world) st_pair(a.ar.data[r] + off, v, flag);
+    }
+  };
   for (int idx = tid; idx < Mc * kStripN; idx += kThreads) {
     const int m = idx / kStripN, nl = idx - m * kStripN;
     float v = 0.f;
@@ -502,39 +533,80 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
                [m * DecGeo<TOKSETS>::kPartStride + nl];
     if (nsplit == 1) {
       const int n = nbase + nl;
-      if (n < a.N) a.out[(int64_t)(m0 + m) * a.ldo + n] = __float2half_rn(v);
+      if (n < a.N) emit(idx, m, n, v);
     } else {
       a.part[(size_t)cta * slot_stride + idx] = v;
     }
   }
-  if (nsplit == 1) return;                             // uniform over the CTA
-
-  // ---- split-K: after the barrier, one thread takes a ticket with an acq_rel atomic
-  // (gpu scope): its release is cumulative over the slot stores the barrier ordered
-  // before it, its acquire (passed on by the next barrier) makes the other CTAs' slots
-  // visible to the last CTA, which sums the tile's slots in slot order ---------------
-  __syncthreads();
-  if (tid == 0) *last_flag = (atom_add_acq_rel_gpu(a.cnt + tile, 1) == nsplit - 1) ? 1 : 0;
-  __syncthreads();
-  if (!*last_flag) return;
-  for (int idx = tid; idx < Mc * kStripN; idx += kThreads) {
-    const int m = idx / kStripN, nl = idx - m * kStripN;
-    const int n = nbase + nl;
-    if (n >= a.N) continue;
-    const float* p = a.part + (size_t)first * slot_stride + idx;
-    float v = 0.f;
-    for (int r0 = 0; r0 < nsplit; r0 += 8) {
-      float v8[8];
+  if (nsplit > 1) {
+    // ---- split-K: after the barrier, one thread takes a ticket with an acq_rel atomic
+    // (gpu scope): its release is cumulative over the slot stores the barrier ordered
+    // before it, its acquire (passed on by the next barrier) makes the other CTAs'
+    // slots visible to the last CTA, which sums the tile's slots in slot order --------
+    __syncthreads();
+    if (tid == 0) *last_flag = (atom_add_acq_rel_gpu(a.cnt + tile, 1) == nsplit - 1) ? 1 : 0;
+    __syncthreads();
+    if (!*last_flag) return;
+    for (int idx = tid; idx < Mc * kStripN; idx += kThreads) {
+      const int m = idx / kStripN, nl = idx - m * kStripN;
+      const int n = nbase + nl;
+      if (n >= a.N) continue;
+      const float* p = a.part + (size_t)first * slot_stride + idx;
+      float v = 0.f;
+      for (int r0 = 0; r0 < nsplit; r0 += 8) {
+        float v8[8];
 #pragma unroll
-      for (int r = 0; r < 8; ++r)                      // independent loads in flight together
-        v8[r] = (r0 + r < nsplit) ? __ldcg(p + (size_t)(r0 + r) * slot_stride) : 0.f;
+        for (int r = 0; r < 8; ++r)                    // independent loads in flight together
+          v8[r] = (r0 + r < nsplit) ? __ldcg(p + (size_t)(r0 + r) * slot_stride) : 0.f;
 #pragma unroll
-      for (int r = 0; r < 8; ++r)
-        if (r0 + r < nsplit) v += v8[r];               // slot order: deterministic
+        for (int r = 0; r < 8; ++r)
+          if (r0 + r < nsplit) v += v8[r];             // slot order: deterministic
+      }
+      emit(idx, m, n, v);
     }
-    a.out[(int64_t)(m0 + m) * a.ldo + n] = __float2half_rn(v);
+    if (tid == 0) a.cnt[tile] = 0;                     // ready for the next call
   }
-  if (tid == 0) a.cnt[tile] = 0;                       // ready for the next call
+  if (!ar) return;
+
+  // ---- fused all-reduce of this tile (tensor parallel): every thread polls, in this
+  // rank's buffer, the {value, flag} pairs of its own elements from every rank until the
+  // flags read this call's number + 1 (bounded wait), then sums the values in rank order:
+  // every rank computes the same bits ----------------------------------------------------
+  {
+    const unsigned long long* mine = a.ar.data[a.ar.rank] + ar_tile;
+    bool late = false;
+    for (int idx = tid; idx < Mc * kStripN; idx += kThreads) {
+      const int m = idx / kStripN, nl = idx - m * kStripN;
+      const int n = nbase + nl;
+      if (n >= a.N) continue;
+      float v = 0.f;
+      for (int r = 0; r < a.ar.world; ++r) {
+        const unsigned long long* p = mine + (size_t)r * ar_rank_stride + idx;
+        uint2 e = ld_pair(p);
+        if (e.y != flag && !late) {
+          const uint64_t t0 = sm100::globaltimer_ns();
+          for (uint32_t it = 0; e.y != flag; ++it) {
+            e = ld_pair(p);
+            if ((it & 63) == 63 && sm100::globaltimer_ns() - t0 > a.ar.timeout_ns) {
+              atomicOr(a.status, kDevErrPeerTimeout);
+              late = true;                             // no more waiting in this thread
+              break;
+            }
+          }
+        }
+        v += __uint_as_float(e.x);                     // rank order
+      }
+      a.out[(int64_t)(m0 + m) * a.ldo + n] = __float2half_rn(v);
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    // the call's last tile moves this rank to the next call number
+    if (atomicAdd(a.ar.state + 1, 1) == a.strips * ((a.M + MP - 1) / MP) - 1) {
+      a.ar.state[1] = 0;
+      a.ar.state[0] += 1;
+    }
+  }
 }
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -656,7 +728,8 @@ bool gemv_tma_supported(const int32_t* qweight, int64_t N, int64_t ldx, const vo
 cudaError_t launch_gemv_tma(const GemvTmaPlan& p, const void* x, int64_t ldx,
                             const int32_t* qweight, const int32_t* qzeros, const void* scales,
                             void* out, int64_t ldo, int M, int N, int K, int group_size,
-                            void* workspace, int* dev_status, cudaStream_t stream) {
+                            void* workspace, int* dev_status, cudaStream_t stream,
+                            const ArArgs* ar) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return cudaErrorNotSupported;
   if (p.ws_bytes > 0 && !workspace) return cudaErrorInvalidValue;
@@ -690,6 +763,12 @@ cudaError_t launch_gemv_tma(const GemvTmaPlan& p, const void* x, int64_t ldx,
   a.ngrp_cta = p.ngrp;
   a.l2pf = pdl_enabled() ? kL2PrefetchStages : 0;
   a.status = dev_status;
+  if (ar) {
+    a.ar = *ar;
+  } else {
+    a.ar = ArArgs{};
+    a.ar.world = 1;
+  }
   return p.toksets == 1 ? launch_t<1>(tm, a, p.grid, p.smem, stream)
                         : launch_t<2>(tm, a, p.grid, p.smem, stream);
 }

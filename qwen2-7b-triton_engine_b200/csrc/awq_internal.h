@@ -62,10 +62,31 @@ struct GemvTmaPlan {
 // Plan of one launch of at most 16 tokens; false when the shape cannot be planned.
 bool plan_gemv_tma(int64_t M, int64_t N, int64_t K, int64_t group_size, int num_sms,
                    GemvTmaPlan* plan);
+
+// All-reduce across the ranks of a tensor-parallel group, fused into the decode kernel's
+// epilogue (awq_tp.cu owns the buffers).  Rank r's receive buffer holds
+//   state  int [2]                                     calls so far, tiles done this call
+//   data   {fp32 value, u32 flag} [2][world][max_tiles][kArTileFloats]
+// In call number e the last CTA of tile t stores every value of its fp32 tile, paired with
+// the flag e + 1, as one 8-byte store into data[e % 2][rank][t] of every rank (peers over
+// NVLink); each thread then polls, in its own buffer, the pairs of its elements from every
+// rank until their flags read e + 1 and sums the values in rank order.  Flags are unique
+// per call, so nothing is reset; two parities let a rank run one call ahead of a peer.
+constexpr int kMaxWorld = 8;
+constexpr int kArTileFloats = 8 * 256;    // tokens per tile x columns per tile
+struct ArArgs {
+  int world;                   // 1: no all-reduce
+  int rank;
+  int max_tiles;
+  unsigned long long* data[kMaxWorld];   // rank r's data region (this rank's own included)
+  int* state;                  // this rank's state words
+  unsigned long long timeout_ns;
+};
 cudaError_t launch_gemv_tma(const GemvTmaPlan& plan, const void* x, int64_t ldx,
                             const int32_t* qweight, const int32_t* qzeros, const void* scales,
                             void* out, int64_t ldo, int M, int N, int K, int group_size,
-                            void* workspace, int* dev_status, cudaStream_t stream);
+                            void* workspace, int* dev_status, cudaStream_t stream,
+                            const ArArgs* ar = nullptr);
 constexpr size_t kGemvTmaMaxSmem = 227 * 1024;   // sm_100's opt-in per-block maximum
 
 // ---- prefill GEMM on tcgen05 / TMEM (awq_gemm_tc.cu) ----------------------------------
@@ -77,7 +98,32 @@ cudaError_t launch_gemm_tc(const void* x, int64_t ldx, const int32_t* qweight,
                            int M, int N, int K, int group_size, int num_sms, int* dev_status,
                            cudaStream_t stream, const char** why);
 
+// Receive-buffer layout of a tensor-parallel communicator (see ArArgs).
+inline size_t tp_data_offset() { return 256; }
+inline size_t tp_buffer_bytes(int world, int max_tiles) {
+  return tp_data_offset() + (size_t)2 * world * max_tiles * kArTileFloats * 8;
+}
+
+}  // namespace awq
+struct awq_tp_comm;
+namespace awq {
+// Kernel arguments of a ready communicator (false when it is not opened).
+bool tp_ar_args(const awq_tp_comm* comm, ArArgs* args);
+
 // Sets the message awq_last_error() returns on this thread; returns `code`.
 int set_last_error(int code, const char* msg);
 
 }  // namespace awq
+
+// Tensor-parallel communicator behind the C ABI's opaque awq_tp_comm (awq_tp.cu).
+struct awq_tp_comm {
+  int device = 0, world = 1, rank = 0;
+  int64_t max_n = 0;
+  int max_tiles = 0;
+  size_t bytes = 0;
+  void* local = nullptr;                   // this rank's receive buffer
+  void* peer[awq::kMaxWorld] = {};         // every rank's buffer as mapped here
+  bool opened[awq::kMaxWorld] = {};        // peer[r] came from cudaIpcOpenMemHandle
+  unsigned long long timeout_ns = 2000000000ull;
+  bool ready = false;                      // awq_tp_comm_open succeeded
+};

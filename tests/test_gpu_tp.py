@@ -95,3 +95,111 @@ def test_tp_world2_matches_single_gpu(cuda, M):
         y, z = res[rank]
         assert O.max_rel_err(y, y_ref) <= TOL, rank
         assert O.max_rel_err(z, z_ref) <= TOL, rank
+
+
+def _fused_worker(rank, world, port, Ms, seed, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    import datetime
+    import sys
+    sys.path.insert(0, os.environ["AWQ_PKG"])
+    sys.path.insert(0, os.environ["AWQ_REPO"])
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60), device_id=dev)
+    comm = None
+    try:
+        import awq_b200
+        from awq_b200 import tp
+        comm = awq_b200.TPComm.from_group(HIDDEN)
+        gu, dn, o = _layers(seed)
+        to = lambda t: tuple(torch.from_numpy(np.ascontiguousarray(a)).to(dev) for a in t)
+        ro = tp.RowParallelAWQ(tp.AWQWeights(*to(o)), world, rank, comm=comm)
+        rd = tp.RowParallelAWQ(tp.AWQWeights(*to(dn)), world, rank, comm=comm)
+        res = {}
+        for M in Ms:
+            x = torch.from_numpy(O.make_x(M, HIDDEN, seed=seed + 3)).to(dev)
+            h = torch.from_numpy(O.make_x(M, INTER, seed=seed + 4)).to(dev)
+            assert ro.comm.supported(x[:, ro.k0:ro.k1].contiguous(), ro.w.qweight, HIDDEN)
+            z = ro(x[:, ro.k0:ro.k1].contiguous())
+            y = rd(h[:, rd.k0:rd.k1].contiguous())
+            res[M] = (z.cpu().numpy(), y.cpu().numpy())
+        # a chain of fused calls replayed from a CUDA graph: o, then down on o's output
+        # (tiled to INTER columns), 3 times, against the same chain run eagerly
+        x = torch.from_numpy(O.make_x(1, HIDDEN, seed=seed + 5)).to(dev)
+
+        def chain():
+            v = x
+            for _ in range(3):
+                z = ro(v[:, ro.k0:ro.k1].contiguous())
+                hh = z.repeat(1, INTER // HIDDEN + 1)[:, :INTER] * 0.05
+                v = rd(hh[:, rd.k0:rd.k1].contiguous())
+            return v
+        eager = chain()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            chain()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            out = chain()
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        st = awq_b200.device_status()
+        q.put((rank, res, eager.cpu().numpy(), out.cpu().numpy(), st))
+        del g
+    finally:
+        torch.cuda.synchronize()
+        if comm is not None:
+            dist.barrier()
+            comm.close()
+        dist.destroy_process_group()
+
+
+def test_fused_allreduce_world2_matches_single_gpu_and_ranks_agree(cuda):
+    """Row-parallel o and down through the fused kernel (product + all-reduce over NVLink
+    peer memory) on 2 GPUs: equal to the single-GPU product within the tolerance, and
+    bit-identical on both ranks (sum in rank order); a graph-replayed chain of fused
+    calls gives the eager chain's bits."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import awq_b200
+    from conftest import PKG, REPO
+    world, seed, Ms = 2, 31, (1, 4, 16)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    os.environ.update(AWQ_PKG=str(PKG), AWQ_REPO=str(REPO))
+    port = _free_port()
+    procs = [ctx.Process(target=_fused_worker, args=(r, world, port, Ms, seed, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in range(world):
+        rank, res, eager, graphed, st = q.get(timeout=300)
+        got[rank] = (res, eager, graphed, st)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    gu, dn, o = _layers(seed)
+    to = lambda t: tuple(torch.from_numpy(np.ascontiguousarray(a)).to(cuda) for a in t)
+    for M in Ms:
+        x = torch.from_numpy(O.make_x(M, HIDDEN, seed=seed + 3)).to(cuda)
+        h = torch.from_numpy(O.make_x(M, INTER, seed=seed + 4)).to(cuda)
+        z_ref = awq_b200.gemm(x, *to(o), 128).float().cpu().numpy()
+        y_ref = awq_b200.gemm(h, *to(dn), 128).float().cpu().numpy()
+        for rank in range(world):
+            z, y = got[rank][0][M]
+            assert O.max_rel_err(z.astype(np.float32), z_ref) <= TOL, (M, rank)
+            assert O.max_rel_err(y.astype(np.float32), y_ref) <= TOL, (M, rank)
+        assert np.array_equal(got[0][0][M][0], got[1][0][M][0])
+        assert np.array_equal(got[0][0][M][1], got[1][0][M][1])
+    for rank in range(world):
+        _, eager, graphed, st = got[rank]
+        assert st == 0
+        assert np.array_equal(eager, graphed)
+    assert np.array_equal(got[0][1], got[1][1])
