@@ -26,6 +26,45 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
+def _start(procs, world):
+    """Start the world-`world` workers with exactly the first `world` GPUs visible to
+    them (the ones they use), whatever the box has."""
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    devs = vis.split(",") if vis else [str(i) for i in range(torch.cuda.device_count())]
+    os.environ["CUDA_VISIBLE_DEVICES"] = ",".join(devs[:world])
+    try:
+        for p in procs:
+            p.start()
+    finally:
+        if vis is None:
+            del os.environ["CUDA_VISIBLE_DEVICES"]
+        else:
+            os.environ["CUDA_VISIBLE_DEVICES"] = vis
+
+
+def _collect(q, procs, world, limit_s=240):
+    """One result per rank from the workers' queue.  A worker that raises sends its
+    traceback instead; a worker that dies or goes silent fails the test within limit_s."""
+    import queue
+    import time
+    got = []
+    t0 = time.monotonic()
+    while len(got) < world:
+        try:
+            item = q.get(timeout=5)
+        except queue.Empty:
+            dead = [p.exitcode for p in procs if p.exitcode not in (None, 0)]
+            if dead:
+                pytest.fail(f"a TP worker exited with {dead} before sending its result")
+            if time.monotonic() - t0 > limit_s:
+                pytest.fail(f"TP workers sent {len(got)} of {world} results in {limit_s} s")
+            continue
+        if isinstance(item, tuple) and item and item[0] == "error":
+            pytest.fail(f"TP worker rank {item[1]} raised:\n{item[2]}")
+        got.append(item)
+    return got
+
+
 def _layers(seed):
     gu = O.make_awq_layer(HIDDEN, 2 * INTER, 128, seed=seed)
     dn = O.make_awq_layer(INTER, HIDDEN, 128, seed=seed + 1)
@@ -57,6 +96,10 @@ def _worker(rank, world, port, M, seed, q):
         z = ro(x[:, ro.k0:ro.k1].contiguous())
         torch.cuda.synchronize()
         q.put((rank, y.float().cpu().numpy(), z.float().cpu().numpy()))
+    except BaseException:
+        import traceback
+        q.put(("error", rank, traceback.format_exc()))
+        raise
     finally:
         dist.destroy_process_group()
 
@@ -74,11 +117,9 @@ def test_tp_world2_matches_single_gpu(cuda, M):
     os.environ.update(env)
     port = _free_port()
     procs = [ctx.Process(target=_worker, args=(r, world, port, M, seed, q)) for r in range(world)]
-    for p in procs:
-        p.start()
+    _start(procs, world)
     res = {}
-    for _ in range(world):
-        rank, y, z = q.get(timeout=300)
+    for rank, y, z in _collect(q, procs, world):
         res[rank] = (y, z)
     for p in procs:
         p.join(timeout=120)
@@ -153,6 +194,10 @@ def _fused_worker(rank, world, port, Ms, seed, q):
         st = awq_b200.device_status()
         q.put((rank, res, eager.cpu().numpy(), out.cpu().numpy(), st))
         del g
+    except BaseException:
+        import traceback
+        q.put(("error", rank, traceback.format_exc()))
+        raise
     finally:
         torch.cuda.synchronize()
         if comm is not None:
@@ -176,11 +221,9 @@ def test_fused_allreduce_world2_matches_single_gpu_and_ranks_agree(cuda):
     os.environ.update(AWQ_PKG=str(PKG), AWQ_REPO=str(REPO))
     port = _free_port()
     procs = [ctx.Process(target=_fused_worker, args=(r, world, port, Ms, seed, q)) for r in range(world)]
-    for p in procs:
-        p.start()
+    _start(procs, world)
     got = {}
-    for _ in range(world):
-        rank, res, eager, graphed, st = q.get(timeout=300)
+    for rank, res, eager, graphed, st in _collect(q, procs, world):
         got[rank] = (res, eager, graphed, st)
     for p in procs:
         p.join(timeout=120)
