@@ -96,14 +96,16 @@ class _DeviceGuard:
             torch.cuda.set_device(self.prev)
 
 
-def workspace_for(device: torch.device, nbytes: int) -> torch.Tensor:
-    """Zero-initialised split-K workspace for (device, current stream), grown on demand.
+def workspace_for(device: torch.device, nbytes: int, stream=None) -> torch.Tensor:
+    """Zero-initialised split-K workspace for (device, stream -- default: the current
+    one), grown on demand.
 
     The kernels leave its arrival counters at zero after every call, so it is
     zeroed once per allocation only.  One workspace per stream keeps concurrent
     streams from sharing counters.
     """
-    stream = torch.cuda.current_stream(device)
+    if stream is None:
+        stream = torch.cuda.current_stream(device)
     key = (device.index, stream.cuda_stream)
     with _ws_lock:
         ws = _workspaces.get(key)
@@ -112,6 +114,49 @@ def workspace_for(device: torch.device, nbytes: int) -> torch.Tensor:
             ws = torch.zeros(size, dtype=torch.uint8, device=device)
             _workspaces[key] = ws
         return ws
+
+
+# Per-call host work that only depends on the weights' metadata or the shape is cached:
+# a decode step issues 112 calls on the same weight tensors.
+_checked_lock = threading.Lock()
+_checked: dict = {}        # weight metadata -> (K, N) of dense, 16-byte aligned weights
+_ws_need: dict = {}        # (device, M, N, K, group_size) -> workspace bytes
+
+
+def _prepared_weights(qweight, qzeros, scales, group_size):
+    """check_weights + _dense16, skipped for weights validated before with the same
+    pointers, shapes, strides, dtypes and device (the checks depend on nothing else).
+    Returns (K, N, qweight, qzeros, scales)."""
+    try:
+        key = (qweight.data_ptr(), qzeros.data_ptr(), scales.data_ptr(), qweight.shape,
+               qzeros.shape, scales.shape, qweight.stride(), qzeros.stride(), scales.stride(),
+               qweight.dtype, qzeros.dtype, scales.dtype, qweight.device, int(group_size))
+    except (AttributeError, TypeError, ValueError):
+        key = None
+    if key is not None:
+        hit = _checked.get(key)
+        if hit is not None:
+            return hit[0], hit[1], qweight, qzeros, scales
+    K, N = check_weights(qweight, qzeros, scales, group_size)
+    dense = [_dense16(t) for t in (qweight, qzeros, scales)]
+    if key is not None and all(d is t for d, t in zip(dense, (qweight, qzeros, scales))):
+        with _checked_lock:
+            if len(_checked) > 65536:
+                _checked.clear()
+            _checked[key] = (K, N)
+    return (K, N, *dense)
+
+
+def _workspace_need(lib, dev: torch.device, M: int, N: int, K: int, group_size: int) -> int:
+    key = (dev.index, M, N, K, group_size)
+    need = _ws_need.get(key)
+    if need is None:
+        need = int(lib.awq_gemm_workspace_bytes(M, N, K, group_size))
+        with _checked_lock:
+            if len(_ws_need) > 65536:
+                _ws_need.clear()
+            _ws_need[key] = need
+    return need
 
 
 def dequant(qweight: torch.Tensor, qzeros: torch.Tensor, scales: torch.Tensor,
@@ -140,34 +185,35 @@ def gemm(x2d: torch.Tensor, qweight: torch.Tensor, qzeros: torch.Tensor, scales:
          group_size: int = 128, path: int = AWQ_PATH_AUTO,
          out: torch.Tensor | None = None) -> torch.Tensor:
     """fp16 [M, N] = x2d fp16 [M, K] @ W with fp32 accumulation, on the current stream."""
-    K, N = check_weights(qweight, qzeros, scales, group_size)
+    K, N, qweight, qzeros, scales = _prepared_weights(qweight, qzeros, scales, group_size)
     _require_cuda(x2d, "x")
     if x2d.dtype != torch.float16:
         raise TypeError(f"x must be float16, got {x2d.dtype}")
     if x2d.dim() != 2 or x2d.shape[1] != K:
         raise ValueError(f"x must be [M, K={K}], got {tuple(x2d.shape)}")
-    if x2d.device != qweight.device:
+    dev = x2d.device
+    if dev != qweight.device:
         raise ValueError("x and the weights must be on one device")
     M = x2d.shape[0]
-    dev = x2d.device
     if out is None:
         out = torch.empty((M, N), dtype=torch.float16, device=dev)
     if M == 0:
         return out
-    qweight, qzeros, scales = _dense16(qweight), _dense16(qzeros), _dense16(scales)
     if x2d.stride(1) != 1 or x2d.data_ptr() % 16 or (x2d.stride(0) * 2) % 16:
         x2d = x2d.contiguous()
         if x2d.data_ptr() % 16:
             x2d = x2d.clone()
     lib = _lib.load()
+    gs = int(group_size)
     with _DeviceGuard(dev):
-        need = lib.awq_gemm_workspace_bytes(M, N, K, int(group_size))
-        ws = workspace_for(dev, need) if need else None
+        stream = torch.cuda.current_stream(dev)
+        need = _workspace_need(lib, dev, M, N, K, gs)
+        ws = workspace_for(dev, need, stream) if need else None
         _lib.check(lib.awq_gemm_f16_ex(
             x2d.data_ptr(), x2d.stride(0), qweight.data_ptr(), qzeros.data_ptr(),
-            scales.data_ptr(), out.data_ptr(), out.stride(0), M, N, K, int(group_size),
+            scales.data_ptr(), out.data_ptr(), out.stride(0), M, N, K, gs,
             ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
-            _stream_handle(dev), int(path)))
+            stream.cuda_stream, int(path)))
     return out
 
 
