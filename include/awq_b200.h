@@ -91,6 +91,20 @@ AWQ_API int awq_gemm_f16_ex(const void* x, int64_t ldx, const int32_t* qweight, 
                     int path);
 
 /*
+ * out = x @ W + bias: the product with the bias of the layer added in its epilogue
+ * (bias fp16 [N], added to every row in fp32 before the one fp16 rounding).  Replaces
+ * the awq_gemm_forward + `out + bias` pair of the reference's biased linears
+ * (model/qwen2.py:45-46 for LinearAWQ, :108-109 for the fused q/k/v), saving the second
+ * kernel and a write and read of the output.  Same kernels and requirements as
+ * awq_gemm_f16 (AWQ_PATH_AUTO).
+ */
+AWQ_API int awq_gemm_f16_bias(const void* x, int64_t ldx, const int32_t* qweight,
+                              const int32_t* qzeros, const void* scales, const void* bias,
+                              void* out, int64_t ldo, int64_t M, int64_t N, int64_t K,
+                              int64_t group_size, void* workspace, size_t workspace_bytes,
+                              void* stream);
+
+/*
  * awq_gemm_f16 for callers that cannot allocate device memory: same inputs and
  * output, no workspace argument.  No counterpart in the reference (its M<=4 path
  * allocates a global K*N buffer, kernels/awq_gemm.py:255-262).  Meant for hosts that

@@ -183,9 +183,17 @@ def dequant(qweight: torch.Tensor, qzeros: torch.Tensor, scales: torch.Tensor,
 
 def gemm(x2d: torch.Tensor, qweight: torch.Tensor, qzeros: torch.Tensor, scales: torch.Tensor,
          group_size: int = 128, path: int = AWQ_PATH_AUTO,
-         out: torch.Tensor | None = None) -> torch.Tensor:
-    """fp16 [M, N] = x2d fp16 [M, K] @ W with fp32 accumulation, on the current stream."""
+         out: torch.Tensor | None = None, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """fp16 [M, N] = x2d fp16 [M, K] @ W (+ bias fp16 [N], added in the kernel's
+    epilogue before the fp16 rounding) with fp32 accumulation, on the current stream."""
     K, N, qweight, qzeros, scales = _prepared_weights(qweight, qzeros, scales, group_size)
+    if bias is not None:
+        _require_cuda(bias, "bias")
+        if bias.dtype != torch.float16 or tuple(bias.shape) != (N,):
+            raise ValueError(f"bias must be float16 [N={N}], got {bias.dtype} {tuple(bias.shape)}")
+        if path != AWQ_PATH_AUTO:
+            raise ValueError("the bias epilogue runs on the automatic kernel choice only")
+        bias = bias.contiguous()
     _require_cuda(x2d, "x")
     if x2d.dtype != torch.float16:
         raise TypeError(f"x must be float16, got {x2d.dtype}")
@@ -209,11 +217,18 @@ def gemm(x2d: torch.Tensor, qweight: torch.Tensor, qzeros: torch.Tensor, scales:
         stream = torch.cuda.current_stream(dev)
         need = _workspace_need(lib, dev, M, N, K, gs)
         ws = workspace_for(dev, need, stream) if need else None
-        _lib.check(lib.awq_gemm_f16_ex(
-            x2d.data_ptr(), x2d.stride(0), qweight.data_ptr(), qzeros.data_ptr(),
-            scales.data_ptr(), out.data_ptr(), out.stride(0), M, N, K, gs,
-            ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
-            stream.cuda_stream, int(path)))
+        if bias is None:
+            _lib.check(lib.awq_gemm_f16_ex(
+                x2d.data_ptr(), x2d.stride(0), qweight.data_ptr(), qzeros.data_ptr(),
+                scales.data_ptr(), out.data_ptr(), out.stride(0), M, N, K, gs,
+                ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
+                stream.cuda_stream, int(path)))
+        else:
+            _lib.check(lib.awq_gemm_f16_bias(
+                x2d.data_ptr(), x2d.stride(0), qweight.data_ptr(), qzeros.data_ptr(),
+                scales.data_ptr(), bias.data_ptr(), out.data_ptr(), out.stride(0), M, N, K, gs,
+                ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
+                stream.cuda_stream))
     return out
 
 

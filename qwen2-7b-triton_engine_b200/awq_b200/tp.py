@@ -33,6 +33,12 @@ def _default_gemm() -> GemmFn:
     return awq_gemm_forward
 
 
+def _default_gemm_bias():
+    """The library product with the bias added in its epilogue (one kernel)."""
+    from kernels.awq_gemm import awq_gemm_bias_forward
+    return awq_gemm_bias_forward
+
+
 def even_split(total: int, parts: int, rank: int) -> tuple[int, int]:
     """[lo, hi) of `rank` when `total` units are dealt as evenly as possible."""
     base, extra = divmod(total, parts)
@@ -113,8 +119,13 @@ class ColumnParallelAWQ:
             bias = torch.cat(pieces)
         self.w = AWQWeights(qw, qz, s, full.group_size, bias)
         self.gemm = gemm or _default_gemm()
+        # the library's product fuses the bias; a substituted product adds it afterwards
+        self.gemm_bias = _default_gemm_bias() if gemm is None else None
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        if self.w.bias is not None and self.gemm_bias is not None:
+            return self.gemm_bias(x, self.w.qweight, self.w.qzeros, self.w.scales, self.w.bias,
+                                  self.w.group_size)
         out = self.gemm(x, self.w.qweight, self.w.qzeros, self.w.scales, self.w.group_size)
         if self.w.bias is not None:                   # bias added after the GEMM (model/qwen2.py:45-46)
             out = out + self.w.bias

@@ -149,10 +149,11 @@ int awq_tc_supported(const void* x, int64_t ldx, const int32_t* qweight, const i
   return awq::tc_supported(x, ldx, qweight, qzeros, scales, M, N, K, group_size) ? 1 : 0;
 }
 
-int awq_gemm_f16_ex(const void* x, int64_t ldx, const int32_t* qweight, const int32_t* qzeros,
-                    const void* scales, void* out, int64_t ldo, int64_t M, int64_t N, int64_t K,
-                    int64_t group_size, void* workspace, size_t workspace_bytes, void* stream,
-                    int path) {
+// The product behind awq_gemm_f16_ex and awq_gemm_f16_bias (bias: fp16 [N] or null).
+static int gemm_impl(const void* x, int64_t ldx, const int32_t* qweight, const int32_t* qzeros,
+                     const void* scales, void* out, int64_t ldo, int64_t M, int64_t N, int64_t K,
+                     int64_t group_size, void* workspace, size_t workspace_bytes, void* stream,
+                     int path, const void* bias) {
   int rc = check_weights(qweight, qzeros, scales, K, N, group_size);
   if (rc) return rc;
   if (!x || !out) return fail(AWQ_ERR_INVALID_ARG, "null x or out");
@@ -179,7 +180,8 @@ int awq_gemm_f16_ex(const void* x, int64_t ldx, const int32_t* qweight, const in
   if (use_tc) {
     const char* why = nullptr;
     cudaError_t e = awq::launch_gemm_tc(x, ldx, qweight, qzeros, scales, out, ldo, (int)M, (int)N,
-                                        (int)K, (int)group_size, d->num_sms, d->status, st, &why);
+                                        (int)K, (int)group_size, d->num_sms, d->status, st, &why,
+                                        bias);
     if (why) return fail(AWQ_ERR_UNSUPPORTED, "tcgen05 path: %s", why);
     if (e != cudaSuccess) return fail_cuda(e, "tcgen05 GEMM launch");
     return AWQ_OK;
@@ -205,7 +207,7 @@ int awq_gemm_f16_ex(const void* x, int64_t ldx, const int32_t* qweight, const in
         cudaError_t e = awq::launch_gemv_tma(mc == m_full ? full : rest, xb + 2 * m0 * ldx, ldx,
                                              qweight, qzeros, scales, ob + 2 * m0 * ldo, ldo, (int)mc,
                                              (int)N, (int)K, (int)group_size, workspace, d->status,
-                                             st);
+                                             st, nullptr, bias);
         if (e != cudaSuccess) return fail_cuda(e, "decode (TMA) kernel launch");
       }
       return AWQ_OK;
@@ -223,9 +225,27 @@ int awq_gemm_f16_ex(const void* x, int64_t ldx, const int32_t* qweight, const in
   if (need > 0 && !aligned16(workspace))
     return fail(AWQ_ERR_INVALID_ARG, "workspace must be 16-byte aligned");
   cudaError_t e = awq::launch_gemv(plan, x, ldx, qweight, qzeros, scales, out, ldo, (int)M, (int)N,
-                                   (int)K, (int)group_size, workspace, st);
+                                   (int)K, (int)group_size, workspace, st, bias);
   if (e != cudaSuccess) return fail_cuda(e, "decode kernel launch");
   return AWQ_OK;
+}
+
+int awq_gemm_f16_ex(const void* x, int64_t ldx, const int32_t* qweight, const int32_t* qzeros,
+                    const void* scales, void* out, int64_t ldo, int64_t M, int64_t N, int64_t K,
+                    int64_t group_size, void* workspace, size_t workspace_bytes, void* stream,
+                    int path) {
+  return gemm_impl(x, ldx, qweight, qzeros, scales, out, ldo, M, N, K, group_size, workspace,
+                   workspace_bytes, stream, path, nullptr);
+}
+
+int awq_gemm_f16_bias(const void* x, int64_t ldx, const int32_t* qweight, const int32_t* qzeros,
+                      const void* scales, const void* bias, void* out, int64_t ldo, int64_t M,
+                      int64_t N, int64_t K, int64_t group_size, void* workspace,
+                      size_t workspace_bytes, void* stream) {
+  if (!bias || (reinterpret_cast<uintptr_t>(bias) & 1))
+    return fail(AWQ_ERR_INVALID_ARG, "bias must be a non-null, 2-byte aligned fp16 [N] pointer");
+  return gemm_impl(x, ldx, qweight, qzeros, scales, out, ldo, M, N, K, group_size, workspace,
+                   workspace_bytes, stream, AWQ_PATH_AUTO, bias);
 }
 
 int awq_gemm_f16(const void* x, int64_t ldx, const int32_t* qweight, const int32_t* qzeros,

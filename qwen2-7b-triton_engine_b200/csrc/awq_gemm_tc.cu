@@ -77,6 +77,7 @@ struct TcArgs {
   int64_t ldo;
   int M, N, K, gs;
   int* status;
+  const __half* bias;   // fp16 [N] added to every output row in fp32, or null
 };
 
 template <int NACC>
@@ -244,6 +245,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         sm100::tmem_ld_wait();
         const int col = tile_n * BN + c * 32;
         if (row < args.M && col < args.N) {
+          if (args.bias) {                      // the columns' bias, added in fp32
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              v[j] = __float_as_uint(__uint_as_float(v[j]) + __half2float(args.bias[col + j]));
+          }
           uint32_t h[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j)
@@ -323,7 +329,7 @@ bool tc_supported(const void* x, int64_t ldx, const int32_t* qweight, const int3
 cudaError_t launch_gemm_tc(const void* x, int64_t ldx, const int32_t* qweight,
                            const int32_t* qzeros, const void* scales, void* out, int64_t ldo,
                            int M, int N, int K, int group_size, int num_sms, int* dev_status,
-                           cudaStream_t stream, const char** why) {
+                           cudaStream_t stream, const char** why, const void* bias) {
   (void)num_sms;
   *why = nullptr;
   if (!tc_supported(x, ldx, qweight, qzeros, scales, M, N, K, group_size)) {
@@ -366,6 +372,7 @@ cudaError_t launch_gemm_tc(const void* x, int64_t ldx, const int32_t* qweight,
   a.ldo = ldo;
   a.M = M; a.N = N; a.K = K; a.gs = group_size;
   a.status = dev_status;
+  a.bias = static_cast<const __half*>(bias);
   dim3 grid((M + BM - 1) / BM, (N + BN - 1) / BN);
   if (nacc == 2)
     gemm_tc_kernel<2><<<grid, kThreads, Geo<2>::SMEM_BYTES, stream>>>(tmA, tmW, tmS, tmZ, a);

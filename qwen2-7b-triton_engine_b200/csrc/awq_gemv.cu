@@ -63,7 +63,14 @@ struct GemvArgs {
   int strips, splits, bps;
   float* ws;        // [zchunks][splits][16][strips*256]
   int* counters;    // [zchunks][strips]
+  const __half* bias;   // fp16 [N] added to every output row in fp32, or null
 };
+
+// Output element: the fp32 sum plus the column's bias (when given), rounded once.
+__device__ __forceinline__ __half out_value(const GemvArgs& a, int n, float v) {
+  if (a.bias) v += __half2float(a.bias[n]);
+  return __float2half_rn(v);
+}
 
 template <bool VEC>
 __device__ __forceinline__ void load_words(const GemvArgs& a, int row, int wc0, uint32_t w[4]) {
@@ -265,7 +272,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
     for (int idx = tid; idx < Mc * kStripN; idx += kGemvThreads) {
       const int m = idx / kStripN, nl = idx - m * kStripN;
       const int n = nbase + nl;
-      if (n < a.N) a.out[(int64_t)(m0 + m) * a.ldo + n] = __float2half_rn(red[m * kRedStride + nl]);
+      if (n < a.N) a.out[(int64_t)(m0 + m) * a.ldo + n] = out_value(a, n, red[m * kRedStride + nl]);
     }
     return;
   }
@@ -288,7 +295,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_kernel(const GemvArgs a) {
     const int n = nbase + nl;
     float v = 0.f;
     for (int sp = 0; sp < a.splits; ++sp) v += __ldcg(base + ((int64_t)sp * 16 + m) * NP + n);
-    if (n < a.N) a.out[(int64_t)(m0 + m) * a.ldo + n] = __float2half_rn(v);
+    if (n < a.N) a.out[(int64_t)(m0 + m) * a.ldo + n] = out_value(a, n, v);
   }
   if (tid == 0) *ctr = 0;                           // leave the counter at zero for the next call
 }
@@ -391,8 +398,10 @@ static void launch_t(const GemvPlan& plan, const GemvArgs& args, int zchunks, cu
 
 cudaError_t launch_gemv(const GemvPlan& plan, const void* x, int64_t ldx, const int32_t* qweight,
                         const int32_t* qzeros, const void* scales, void* out, int64_t ldo, int M,
-                        int N, int K, int group_size, void* workspace, cudaStream_t stream) {
+                        int N, int K, int group_size, void* workspace, cudaStream_t stream,
+                        const void* bias) {
   GemvArgs a;
+  a.bias = static_cast<const __half*>(bias);
   a.ldx = ldx;
   a.qw = qweight;
   a.qz = qzeros;

@@ -101,6 +101,7 @@ struct TmaGemvArgs {
   int l2pf;        // weight stages each warp prefetches into L2 before the dependency wait
   int* status;
   ArArgs ar;       // fused all-reduce across tensor-parallel ranks (ar.world == 1: none)
+  const __half* bias;   // fp16 [N] added to every output row in fp32, or null
 };
 
 __device__ __forceinline__ void mma_16816(float c[4], uint32_t a0, uint32_t a1, uint32_t a2,
@@ -514,9 +515,14 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
   const uint32_t flag = epoch + 1u;
   const size_t ar_rank_stride = (size_t)a.ar.max_tiles * kArTileFloats;
   const size_t ar_tile = ((size_t)(epoch & 1u) * a.ar.world * a.ar.max_tiles + tile) * kArTileFloats;
+  // fp32 sum plus the column's bias (when given), rounded once
+  auto out_value = [&](int n, float v) {
+    if (a.bias) v += __half2float(a.bias[n]);
+    return __float2half_rn(v);
+  };
   auto emit = [&](int idx, int m, int n, float v) {
     if (!ar) {
-      a.out[(int64_t)(m0 + m) * a.ldo + n] = __float2half_rn(v);
+      a.out[(int64_t)(m0 + m) * a.ldo + n] = out_value(n, v);
     } else {
       const size_t off = ar_tile + (size_t)a.ar.rank * ar_rank_stride + idx;
 #pragma unroll
@@ -596,7 +602,7 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
         }
         v += __uint_as_float(e.x);                     // rank order
       }
-      a.out[(int64_t)(m0 + m) * a.ldo + n] = __float2half_rn(v);
+      a.out[(int64_t)(m0 + m) * a.ldo + n] = out_value(n, v);
     }
   }
   __syncthreads();
@@ -729,7 +735,7 @@ cudaError_t launch_gemv_tma(const GemvTmaPlan& p, const void* x, int64_t ldx,
                             const int32_t* qweight, const int32_t* qzeros, const void* scales,
                             void* out, int64_t ldo, int M, int N, int K, int group_size,
                             void* workspace, int* dev_status, cudaStream_t stream,
-                            const ArArgs* ar) {
+                            const ArArgs* ar, const void* bias) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return cudaErrorNotSupported;
   if (p.ws_bytes > 0 && !workspace) return cudaErrorInvalidValue;
@@ -763,6 +769,7 @@ cudaError_t launch_gemv_tma(const GemvTmaPlan& p, const void* x, int64_t ldx,
   a.ngrp_cta = p.ngrp;
   a.l2pf = pdl_enabled() ? kL2PrefetchStages : 0;
   a.status = dev_status;
+  a.bias = static_cast<const __half*>(bias);
   if (ar) {
     a.ar = *ar;
   } else {

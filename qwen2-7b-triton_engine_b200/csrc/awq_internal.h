@@ -40,9 +40,12 @@ size_t gemv_workspace_bytes(const GemvPlan& plan);
 // bytes; false if even the smallest plan does not fit.
 bool plan_gemv_bounded(int64_t M, int64_t N, int64_t K, int64_t group_size, int num_sms,
                        bool vec_ok, size_t max_workspace, GemvPlan* plan);
+// `bias` (fp16 [N] or null) is added to every output row in fp32 before the fp16 rounding,
+// here and in the other product kernels.
 cudaError_t launch_gemv(const GemvPlan& plan, const void* x, int64_t ldx, const int32_t* qweight,
                         const int32_t* qzeros, const void* scales, void* out, int64_t ldo, int M,
-                        int N, int K, int group_size, void* workspace, cudaStream_t stream);
+                        int N, int K, int group_size, void* workspace, cudaStream_t stream,
+                        const void* bias = nullptr);
 
 // ---- decode on mma.sync with TMA streaming, one CTA per SM (awq_gemv_tma.cu) ---------
 // Shapes TMA can describe (N % 32 == 0, 16-byte aligned qweight and x, ldx % 8 == 0).
@@ -86,7 +89,7 @@ cudaError_t launch_gemv_tma(const GemvTmaPlan& plan, const void* x, int64_t ldx,
                             const int32_t* qweight, const int32_t* qzeros, const void* scales,
                             void* out, int64_t ldo, int M, int N, int K, int group_size,
                             void* workspace, int* dev_status, cudaStream_t stream,
-                            const ArArgs* ar = nullptr);
+                            const ArArgs* ar = nullptr, const void* bias = nullptr);
 constexpr size_t kGemvTmaMaxSmem = 227 * 1024;   // sm_100's opt-in per-block maximum
 
 // ---- prefill GEMM on tcgen05 / TMEM (awq_gemm_tc.cu) ----------------------------------
@@ -96,7 +99,7 @@ bool tc_supported(const void* x, int64_t ldx, const int32_t* qweight, const int3
 cudaError_t launch_gemm_tc(const void* x, int64_t ldx, const int32_t* qweight,
                            const int32_t* qzeros, const void* scales, void* out, int64_t ldo,
                            int M, int N, int K, int group_size, int num_sms, int* dev_status,
-                           cudaStream_t stream, const char** why);
+                           cudaStream_t stream, const char** why, const void* bias = nullptr);
 
 // Receive-buffer layout of a tensor-parallel communicator (see ArArgs).
 inline size_t tp_data_offset() { return 256; }

@@ -11,6 +11,9 @@ directory first on ``sys.path`` (``import kernels.awq_gemm``) or assign
   sm_100a decode kernel (mma.sync, split-K); larger M runs the tcgen05/TMEM prefill
   GEMM.  Differences: inputs are validated up front (TypeError / ValueError), a CPU
   tensor raises instead of running, and no global K*N fp16 buffer is kept.
+* ``awq_gemm_bias_forward(x, qweight, qzeros, scales, bias, group_size=128)`` -- not in
+  the reference: the product plus the layer's bias in one kernel, for the callers that
+  add the bias afterwards (``model/qwen2.py:45-46,108-109``).
 * ``_dequant_to_fp16(qweight, qzeros, scales, out_buf, group_size=128)`` --
   reference ``kernels/awq_gemm.py:66-87``; writes the bit-identical fp16 weights.
 """
@@ -20,7 +23,7 @@ import torch
 
 import awq_b200
 
-__all__ = ["awq_gemm_forward", "_dequant_to_fp16"]
+__all__ = ["awq_gemm_forward", "awq_gemm_bias_forward", "_dequant_to_fp16"]
 
 
 def _dequant_to_fp16(qweight: torch.Tensor, qzeros: torch.Tensor, scales: torch.Tensor,
@@ -43,4 +46,22 @@ def awq_gemm_forward(x: torch.Tensor, qweight: torch.Tensor, qzeros: torch.Tenso
     x_flat = x.reshape(-1, x.shape[-1])
     N = scales.shape[1]
     out = awq_b200.gemm(x_flat, qweight, qzeros, scales, group_size)
+    return out.view(*in_shape[:-1], N)
+
+
+def awq_gemm_bias_forward(x: torch.Tensor, qweight: torch.Tensor, qzeros: torch.Tensor,
+                          scales: torch.Tensor, bias: torch.Tensor,
+                          group_size: int = 128) -> torch.Tensor:
+    """``awq_gemm_forward(x, ...) + bias`` in one kernel: the bias (fp16 [N]) is added in
+    the product's epilogue.  For the reference's biased call sites, which add the bias
+    after the product (``model/qwen2.py:45-46``, ``:108-109``).  Not in the reference
+    module; the result differs from the two-step form only by its single fp16 rounding."""
+    if not isinstance(x, torch.Tensor):
+        raise TypeError("x must be a torch.Tensor")
+    if x.dim() < 1:
+        raise ValueError("x must have at least one dimension")
+    in_shape = x.shape
+    x_flat = x.reshape(-1, x.shape[-1])
+    N = scales.shape[1]
+    out = awq_b200.gemm(x_flat, qweight, qzeros, scales, group_size, bias=bias)
     return out.view(*in_shape[:-1], N)

@@ -242,3 +242,31 @@ def test_chained_calls_read_the_previous_output(cuda, M):
     for w in layers:
         h = (h.half().float() @ awq_b200.dequant(*w, 128).float())
     assert O.max_rel_err(ref.float().cpu().numpy(), h.cpu().numpy()) <= 3 * TOL
+
+
+@pytest.mark.parametrize("M,K,N,gs", [
+    (1, 3584, 4608, 128),     # decode kernel, split tiles (fused q/k/v shape)
+    (4, 3584, 4608, 128),     # decode kernel, 4 tokens
+    (16, 1024, 1024, 128),    # decode kernel, 8-token chunks
+    (1, 512, 37888, 128),     # decode kernel, one CTA per tile
+    (5, 384, 136, 128),       # generic decode kernel (ragged N)
+    (300, 1024, 1024, 128),   # tcgen05 prefill kernel
+])
+def test_bias_epilogue(cuda, M, K, N, gs):
+    """awq_gemm_bias_forward = product + bias in one kernel (model/qwen2.py:45-46,108-109):
+    within the tolerance of the fp32 oracle plus bias, and of the two-step GPU form."""
+    import awq_b200
+    from kernels import awq_gemm
+    qw, qz, s = O.make_awq_layer(K, N, gs, seed=M + N)
+    x = O.make_x(M, K, seed=K)
+    b = np.random.default_rng(7).uniform(-2, 2, size=N).astype(np.float16)
+    ref = O.awq_gemm_f32(x, qw, qz, s, gs) + b.astype(np.float32)
+    dx, dqw, dqz, ds, db = (torch.from_numpy(a).to(cuda) for a in (x, qw, qz, s, b))
+    out = awq_gemm.awq_gemm_bias_forward(dx, dqw, dqz, ds, db, gs)
+    assert out.shape == (M, N) and out.dtype == torch.float16
+    assert O.max_rel_err(out.float().cpu().numpy(), ref) <= TOL
+    two_step = awq_b200.gemm(dx, dqw, dqz, ds, gs).float() + db.float()
+    assert O.max_rel_err(out.float().cpu().numpy(), two_step.cpu().numpy()) <= TOL
+    assert awq_b200.device_status() == 0
+    with pytest.raises(ValueError):
+        awq_gemm.awq_gemm_bias_forward(dx, dqw, dqz, ds, db[:-8], gs)
