@@ -559,14 +559,15 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
       if (n >= a.N) continue;
       const float* p = a.part + (size_t)first * slot_stride + idx;
       float v = 0.f;
-      for (int r0 = 0; r0 < nsplit; r0 += 8) {
-        float v8[8];
+      // 16 independent loads in flight together: one round trip to L2 for up to 16 slots
+      for (int r0 = 0; r0 < nsplit; r0 += 16) {
+        float v16[16];
 #pragma unroll
-        for (int r = 0; r < 8; ++r)                    // independent loads in flight together
-          v8[r] = (r0 + r < nsplit) ? __ldcg(p + (size_t)(r0 + r) * slot_stride) : 0.f;
+        for (int r = 0; r < 16; ++r)
+          v16[r] = (r0 + r < nsplit) ? __ldcg(p + (size_t)(r0 + r) * slot_stride) : 0.f;
 #pragma unroll
-        for (int r = 0; r < 8; ++r)
-          if (r0 + r < nsplit) v += v8[r];             // slot order: deterministic
+        for (int r = 0; r < 16; ++r)
+          if (r0 + r < nsplit) v += v16[r];            // slot order: deterministic
       }
       emit(idx, m, n, v);
     }
