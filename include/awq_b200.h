@@ -43,7 +43,8 @@ extern "C" {
 #define AWQ_ERR_DEVICE (-5)        /* a kernel reported an error (awq_device_status) */
 
 /* Kernel choice for awq_gemm_f16_ex. */
-#define AWQ_PATH_AUTO 0   /* M <= 16: decode kernel; larger M: tcgen05 GEMM when the shape allows */
+#define AWQ_PATH_AUTO 0   /* M <= 16: decode kernel; larger M: tcgen05 GEMM when the shape allows
+                             and it fills at least half the SMs or M > 64, else decode   */
 #define AWQ_PATH_DECODE 1 /* mma.sync split-K streaming kernel, any M (16-token chunks)          */
 #define AWQ_PATH_TC 2     /* tcgen05/TMEM prefill GEMM; AWQ_ERR_UNSUPPORTED if shape disallows   */
 

@@ -174,7 +174,15 @@ static int gemm_impl(const void* x, int64_t ldx, const int32_t* qweight, const i
                   (long long)M, (long long)N, (long long)K, (long long)group_size);
     use_tc = true;
   } else if (path == AWQ_PATH_AUTO) {
-    use_tc = M > 16 && awq::tc_supported(x, ldx, qweight, qzeros, scales, M, N, K, group_size);
+    // The tcgen05 kernel has no split-K: it runs ceil(M / BM) x ceil(N / 256) CTAs (BM 128,
+    // or 256 above M = 128).  With few of them (o, q/k/v, down at small M) the decode
+    // kernel, in 16-token launches, is faster up to M = 64 (measured on B200: down at
+    // M = 24 / 32 takes 55 / 63 us there against 173 us with 14 tcgen05 CTAs; gate+up with
+    // 148 CTAs is faster on tcgen05 from M = 16 on).
+    const int64_t bm = M > 128 ? 256 : 128;
+    const int64_t tc_ctas = ((M + bm - 1) / bm) * ((N + 255) / 256);
+    use_tc = M > 16 && (M > 64 || 2 * tc_ctas >= d->num_sms) &&
+             awq::tc_supported(x, ldx, qweight, qzeros, scales, M, N, K, group_size);
   }
 
   if (use_tc) {
