@@ -44,7 +44,8 @@ extern "C" {
 
 /* Kernel choice for awq_gemm_f16_ex. */
 #define AWQ_PATH_AUTO 0   /* M <= 16: decode kernel; larger M: tcgen05 GEMM when the shape allows
-                             and it fills at least half the SMs or M > 64, else decode   */
+                             and its CTAs (output tiles x K splits, the splits needing the
+                             workspace) fill at least half the SMs or M > 64, else decode   */
 #define AWQ_PATH_DECODE 1 /* mma.sync split-K streaming kernel, any M (16-token chunks)          */
 #define AWQ_PATH_TC 2     /* tcgen05/TMEM prefill GEMM; AWQ_ERR_UNSUPPORTED if shape disallows   */
 

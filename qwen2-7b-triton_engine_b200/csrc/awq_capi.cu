@@ -133,6 +133,11 @@ size_t awq_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t group_s
     if (mc > 0 && awq::plan_gemv_tma(mc, N, K, group_size, d->num_sms, &tp) && tp.ws_bytes > need)
       need = tp.ws_bytes;
   }
+  // tcgen05 kernel's split-K partials
+  if (M > 16) {
+    const size_t tc = awq::tc_workspace_bytes(M, N, K, d->num_sms);
+    if (tc > need) need = tc;
+  }
   return need;
 }
 
@@ -174,13 +179,17 @@ static int gemm_impl(const void* x, int64_t ldx, const int32_t* qweight, const i
                   (long long)M, (long long)N, (long long)K, (long long)group_size);
     use_tc = true;
   } else if (path == AWQ_PATH_AUTO) {
-    // The tcgen05 kernel has no split-K: it runs ceil(M / BM) x ceil(N / 256) CTAs (BM 128,
-    // or 256 above M = 128).  With few of them (o, q/k/v, down at small M) the decode
-    // kernel, in 16-token launches, is faster up to M = 64 (measured on B200: down at
-    // M = 24 / 32 takes 55 / 63 us there against 173 us with 14 tcgen05 CTAs; gate+up with
-    // 148 CTAs is faster on tcgen05 from M = 16 on).
+    // The tcgen05 kernel runs ceil(M / BM) x ceil(N / 256) output tiles (BM 128, or 256
+    // above M = 128), split along K when they cannot fill the GPU and the workspace holds
+    // the partials.  Without the split, few tiles (o, q/k/v, down at small M) lose to the
+    // decode kernel in 16-token launches up to M = 64 (measured on B200: down at M = 24 /
+    // 32 takes 55 / 63 us there against 173 us with 14 unsplit tcgen05 CTAs, 26 / 27 us
+    // split ten ways).
     const int64_t bm = M > 128 ? 256 : 128;
-    const int64_t tc_ctas = ((M + bm - 1) / bm) * ((N + 255) / 256);
+    int64_t tc_ctas = ((M + bm - 1) / bm) * ((N + 255) / 256);
+    const size_t tc_need = awq::tc_workspace_bytes(M, N, K, d->num_sms);
+    if (tc_need > 0 && workspace && workspace_bytes >= tc_need)
+      tc_ctas *= awq::tc_splits(M, N, K, d->num_sms);
     use_tc = M > 16 && (M > 64 || 2 * tc_ctas >= d->num_sms) &&
              awq::tc_supported(x, ldx, qweight, qzeros, scales, M, N, K, group_size);
   }
@@ -189,7 +198,7 @@ static int gemm_impl(const void* x, int64_t ldx, const int32_t* qweight, const i
     const char* why = nullptr;
     cudaError_t e = awq::launch_gemm_tc(x, ldx, qweight, qzeros, scales, out, ldo, (int)M, (int)N,
                                         (int)K, (int)group_size, d->num_sms, d->status, st, &why,
-                                        bias);
+                                        bias, workspace, workspace_bytes);
     if (why) return fail(AWQ_ERR_UNSUPPORTED, "tcgen05 path: %s", why);
     if (e != cudaSuccess) return fail_cuda(e, "tcgen05 GEMM launch");
     return AWQ_OK;

@@ -78,6 +78,8 @@ struct TcArgs {
   int M, N, K, gs;
   int* status;
   const __half* bias;   // fp16 [N] added to every output row in fp32, or null
+  int splits;           // CTAs along K per output tile (blockIdx.z); > 1: fp32 partials
+  float* part;          // [splits][M][N] fp32 partials when splits > 1
 };
 
 template <int NACC>
@@ -98,7 +100,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int tile_m = blockIdx.x, tile_n = blockIdx.y;
-  const int KT = args.K / BK;
+  // this CTA's K steps [kt0, kt0 + KT) (split-K over blockIdx.z; the ranges of one tile
+  // differ by at most one step); the rings below count steps from 0 within the range
+  const int kt_all = args.K / BK;
+  const int kt0 = (int)((int64_t)blockIdx.z * kt_all / args.splits);
+  const int KT = (int)((int64_t)(blockIdx.z + 1) * kt_all / args.splits) - kt0;
 
   auto bar_tfull = [&](int s) { return sbase + OFF_BAR + 8u * s; };
   auto bar_tempty = [&](int s) { return sbase + OFF_BAR + 8u * (TSTAGES + s); };
@@ -146,7 +152,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           break;
         }
         if (*abort_flag) break;
-        const int k0 = kt * BK;
+        const int k0 = (kt0 + kt) * BK;
         const int grp = k0 / args.gs;
         const uint32_t st = sbase + OFF_T + s * T_STAGE;
         sm100::mbar_arrive_expect_tx(bar_tfull(s), TX_BYTES);
@@ -244,7 +250,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         sm100::tmem_ld_32x32b_x32(taddr + c * 32, v);
         sm100::tmem_ld_wait();
         const int col = tile_n * BN + c * 32;
-        if (row < args.M && col < args.N) {
+        if (row < args.M && col < args.N && args.splits > 1) {
+          // split-K: this CTA's fp32 partial, summed (with the bias) by the reduce kernel
+          float4* dst = reinterpret_cast<float4*>(
+              args.part + ((size_t)blockIdx.z * args.M + row) * args.N + col);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            dst[j] = make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
+                                 __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
+        } else if (row < args.M && col < args.N) {
           if (args.bias) {                      // the columns' bias, added in fp32
 #pragma unroll
             for (int j = 0; j < 32; ++j)
@@ -314,7 +328,49 @@ bool make_map_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* ptr, uint64
 
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+// out[M, N] = fp16(sum over z of part[z] (+ bias)), four columns per thread, z in order.
+__global__ void __launch_bounds__(256)
+tc_splitk_reduce(const float* __restrict__ part, int splits, int M, int N,
+                 __half* __restrict__ out, int64_t ldo, const __half* __restrict__ bias) {
+  const int n4 = N / 4;
+  const int64_t total = (int64_t)M * n4;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = i / n4;
+    const int c = (int)(i - row * n4) * 4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int z = 0; z < splits; ++z) {
+      const float4 v = __ldcs(reinterpret_cast<const float4*>(part + ((size_t)z * M + row) * N + c));
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+    if (bias) {
+      acc.x += __half2float(bias[c]); acc.y += __half2float(bias[c + 1]);
+      acc.z += __half2float(bias[c + 2]); acc.w += __half2float(bias[c + 3]);
+    }
+    const __half2 lo = __floats2half2_rn(acc.x, acc.y), hi = __floats2half2_rn(acc.z, acc.w);
+    *reinterpret_cast<uint2*>(out + row * ldo + c) = make_uint2(h2_as_u32(lo), h2_as_u32(hi));
+  }
+}
+
 }  // namespace
+
+// Split-K factor of the tcgen05 kernel: 1 when its output tiles already fill half the
+// SMs; otherwise as many CTAs per tile as the SMs allow, at most 16, each with at least
+// 8 K steps (512 rows) so that its pipeline still fills.
+int tc_splits(int64_t M, int64_t N, int64_t K, int num_sms) {
+  const int64_t bm = M > 128 ? 256 : 128;
+  const int64_t tiles = ((M + bm - 1) / bm) * ((N + BN - 1) / BN);
+  if (tiles <= 0 || 2 * tiles >= num_sms) return 1;
+  int64_t s = num_sms / tiles;
+  if (s > K / BK / 8) s = K / BK / 8;
+  if (s > 16) s = 16;
+  return s < 1 ? 1 : (int)s;
+}
+
+size_t tc_workspace_bytes(int64_t M, int64_t N, int64_t K, int num_sms) {
+  const int s = tc_splits(M, N, K, num_sms);
+  return s > 1 ? kCounterRegionBytes + (size_t)s * M * N * sizeof(float) : 0;
+}
 
 bool tc_supported(const void* x, int64_t ldx, const int32_t* qweight, const int32_t* qzeros,
                   const void* scales, int64_t M, int64_t N, int64_t K, int64_t group_size) {
@@ -329,8 +385,8 @@ bool tc_supported(const void* x, int64_t ldx, const int32_t* qweight, const int3
 cudaError_t launch_gemm_tc(const void* x, int64_t ldx, const int32_t* qweight,
                            const int32_t* qzeros, const void* scales, void* out, int64_t ldo,
                            int M, int N, int K, int group_size, int num_sms, int* dev_status,
-                           cudaStream_t stream, const char** why, const void* bias) {
-  (void)num_sms;
+                           cudaStream_t stream, const char** why, const void* bias,
+                           void* workspace, size_t workspace_bytes) {
   *why = nullptr;
   if (!tc_supported(x, ldx, qweight, qzeros, scales, M, N, K, group_size)) {
     *why = "shape or alignment not supported";
@@ -373,11 +429,24 @@ cudaError_t launch_gemm_tc(const void* x, int64_t ldx, const int32_t* qweight,
   a.M = M; a.N = N; a.K = K; a.gs = group_size;
   a.status = dev_status;
   a.bias = static_cast<const __half*>(bias);
-  dim3 grid((M + BM - 1) / BM, (N + BN - 1) / BN);
+  // split-K when the caller's workspace holds the partials (after the decode kernels'
+  // counter region, which must stay zero); otherwise one CTA per tile
+  a.splits = tc_splits(M, N, K, num_sms);
+  a.part = nullptr;
+  if (a.splits > 1) {
+    if (workspace && al16(workspace) && workspace_bytes >= tc_workspace_bytes(M, N, K, num_sms))
+      a.part = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterRegionBytes);
+    else
+      a.splits = 1;
+  }
+  dim3 grid((M + BM - 1) / BM, (N + BN - 1) / BN, a.splits);
   if (nacc == 2)
     gemm_tc_kernel<2><<<grid, kThreads, Geo<2>::SMEM_BYTES, stream>>>(tmA, tmW, tmS, tmZ, a);
   else
     gemm_tc_kernel<1><<<grid, kThreads, Geo<1>::SMEM_BYTES, stream>>>(tmA, tmW, tmS, tmZ, a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || a.splits == 1) return e;
+  tc_splitk_reduce<<<num_sms * 4, 256, 0, stream>>>(a.part, a.splits, M, N, a.out, ldo, a.bias);
   return cudaGetLastError();
 }
 

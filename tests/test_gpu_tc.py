@@ -99,3 +99,47 @@ def test_tc_matches_decode_path(cuda):
     a = awq_b200.gemm(dx, dqw, dqz, ds, 128, path=awq_b200.AWQ_PATH_TC).float()
     b = awq_b200.gemm(dx, dqw, dqz, ds, 128, path=awq_b200.AWQ_PATH_DECODE).float()
     assert O.max_rel_err(a.cpu().numpy(), b.cpu().numpy()) <= TOL
+
+
+@pytest.mark.parametrize("M,K,N", [
+    (128, 18944, 3584),     # down shape: 14 tiles -> 10 CTAs per tile along K
+    (40, 3584, 3584),       # o shape at small M: 14 tiles -> 7 per tile
+    (300, 3584, 4608),      # fused q/k/v at M = 300: 36 tiles of 256 rows -> 4 per tile
+])
+def test_tc_split_k(cuda, M, K, N):
+    """Few output tiles: the tcgen05 kernel splits K over several CTAs per tile, writes
+    fp32 partials into the workspace and a reduce kernel sums them in split order.
+    Checked against the CPU oracle on three 64-column blocks and against an fp32 product
+    of the exactly dequantized weights everywhere; repeated calls give the same bits; the
+    bias goes through the reduce kernel; without a workspace the kernel runs unsplit."""
+    import ctypes
+    import awq_b200
+    import awq_b200._lib as L
+    qw, qz, s = O.make_awq_layer(K, N, 128, seed=M * 3 + N)
+    x = O.make_x(M, K, seed=M)
+    dx, dqw, dqz, ds = _dev(cuda, x, qw, qz, s)
+    lib = L.load()
+    assert lib.awq_gemm_workspace_bytes(M, N, K, 128) > 0      # the split's partials
+    a = awq_b200.gemm(dx, dqw, dqz, ds, 128, path=awq_b200.AWQ_PATH_TC)
+    b = awq_b200.gemm(dx, dqw, dqz, ds, 128, path=awq_b200.AWQ_PATH_TC)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+    for c0 in (0, (N // 2) // 64 * 64, N - 64):
+        ref = O.awq_gemm_f32(x, qw[:, c0 // 8:(c0 + 64) // 8], qz[:, c0 // 8:(c0 + 64) // 8],
+                             s[:, c0:c0 + 64], 128)
+        assert O.max_rel_err(a[:, c0:c0 + 64].float().cpu().numpy(), ref) <= TOL, c0
+    full = dx.float() @ awq_b200.dequant(dqw, dqz, ds, 128).float()
+    assert O.max_rel_err(a.float().cpu().numpy(), full.cpu().numpy()) <= TOL
+    bias = torch.from_numpy(np.random.default_rng(3).uniform(-1, 1, N).astype(np.float16)).to(cuda)
+    ab = awq_b200.gemm(dx, dqw, dqz, ds, 128, bias=bias)
+    assert O.max_rel_err(ab.float().cpu().numpy(), (full + bias.float()).cpu().numpy()) <= TOL
+    # no workspace: one CTA per tile, same result within the tolerance
+    out = torch.empty((M, N), dtype=torch.float16, device=cuda)
+    rc = lib.awq_gemm_f16_ex(dx.data_ptr(), K, dqw.data_ptr(), dqz.data_ptr(), ds.data_ptr(),
+                             out.data_ptr(), N, M, N, K, 128, None, 0,
+                             ctypes.c_void_p(torch.cuda.current_stream().cuda_stream),
+                             awq_b200.AWQ_PATH_TC)
+    assert rc == 0, lib.awq_last_error()
+    torch.cuda.synchronize()
+    assert O.max_rel_err(out.float().cpu().numpy(), full.cpu().numpy()) <= TOL
+    assert awq_b200.device_status() == 0
