@@ -43,11 +43,15 @@ extern "C" {
 #define AWQ_ERR_DEVICE (-5)        /* a kernel reported an error (awq_device_status) */
 
 /* Kernel choice for awq_gemm_f16_ex. */
-#define AWQ_PATH_AUTO 0   /* M <= 16: decode kernel; larger M: tcgen05 GEMM when the shape allows
-                             and its CTAs (output tiles x K splits, the splits needing the
-                             workspace) fill at least half the SMs or M > 64, else decode   */
+#define AWQ_PATH_AUTO 0   /* M <= 8: decode kernel; 9..16: small-M tcgen05 kernel (AWQ_PATH_TS)
+                             when the shape allows, else decode; larger M: tcgen05 GEMM when
+                             the shape allows and its CTAs (output tiles x K splits, the
+                             splits needing the workspace) fill at least half the SMs or
+                             M > 64, else decode                                            */
 #define AWQ_PATH_DECODE 1 /* mma.sync split-K streaming kernel, any M (16-token chunks)          */
 #define AWQ_PATH_TC 2     /* tcgen05/TMEM prefill GEMM; AWQ_ERR_UNSUPPORTED if shape disallows   */
+#define AWQ_PATH_TS 3     /* tcgen05 small-M GEMM (M <= 64): weights dequantized into TMEM as the
+                             MMA's A operand, tokens as its N; AWQ_ERR_UNSUPPORTED otherwise    */
 
 /* Library version: major * 10000 + minor * 100 + patch. */
 AWQ_API int awq_version(void);

@@ -19,11 +19,11 @@ import threading
 import torch
 
 from . import _lib
-from ._lib import (AWQ_PATH_AUTO, AWQ_PATH_DECODE, AWQ_PATH_TC, AwqError,  # noqa: F401
+from ._lib import (AWQ_PATH_AUTO, AWQ_PATH_DECODE, AWQ_PATH_TC, AWQ_PATH_TS, AwqError,  # noqa: F401
                    LIB_PATH)
 
 __all__ = ["dequant", "gemm", "gemm_allreduce", "TPComm", "device_status", "workspace_for", "AwqError",
-           "AWQ_PATH_AUTO", "AWQ_PATH_DECODE", "AWQ_PATH_TC", "LIB_PATH"]
+           "AWQ_PATH_AUTO", "AWQ_PATH_DECODE", "AWQ_PATH_TC", "AWQ_PATH_TS", "LIB_PATH"]
 
 _ws_lock = threading.Lock()
 _workspaces: dict = {}

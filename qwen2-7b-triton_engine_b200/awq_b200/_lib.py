@@ -23,6 +23,7 @@ AWQ_ERR_DEVICE = -5
 AWQ_PATH_AUTO = 0
 AWQ_PATH_DECODE = 1
 AWQ_PATH_TC = 2
+AWQ_PATH_TS = 3
 
 # Every symbol include/awq_b200.h declares, with its ctypes signature.
 _P = ctypes.c_void_p

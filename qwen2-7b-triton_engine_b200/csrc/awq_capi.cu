@@ -133,10 +133,14 @@ size_t awq_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t group_s
     if (mc > 0 && awq::plan_gemv_tma(mc, N, K, group_size, d->num_sms, &tp) && tp.ws_bytes > need)
       need = tp.ws_bytes;
   }
-  // tcgen05 kernel's split-K partials
+  // tcgen05 kernels' split-K partials
   if (M > 16) {
     const size_t tc = awq::tc_workspace_bytes(M, N, K, d->num_sms);
     if (tc > need) need = tc;
+  }
+  if (M <= 64) {
+    const size_t ts = awq::ts_workspace_bytes(M, N, K, d->num_sms);
+    if (ts > need) need = ts;
   }
   return need;
 }
@@ -166,11 +170,37 @@ static int gemm_impl(const void* x, int64_t ldx, const int32_t* qweight, const i
   if (ldx < K || ldo < N) return fail(AWQ_ERR_INVALID_ARG, "ldx < K or ldo < N");
   if ((reinterpret_cast<uintptr_t>(x) & 1) || (reinterpret_cast<uintptr_t>(out) & 1))
     return fail(AWQ_ERR_INVALID_ARG, "x and out must be 2-byte aligned");
-  if (path != AWQ_PATH_AUTO && path != AWQ_PATH_DECODE && path != AWQ_PATH_TC)
+  if (path != AWQ_PATH_AUTO && path != AWQ_PATH_DECODE && path != AWQ_PATH_TC &&
+      path != AWQ_PATH_TS)
     return fail(AWQ_ERR_INVALID_ARG, "unknown path %d", path);
   DeviceInfo* d = nullptr;
   if ((rc = device_info(&d))) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  // Small-M tcgen05 kernel (weights dequantized into TMEM): measured on B200 it beats the
+  // decode kernel from 9 to 16 tokens on every Qwen2-7B shape (M = 9: o 11.0 vs 14.8 us,
+  // gate+up 37.0 vs 48.0, down 24.9 vs 31.5; the decode kernel reads the weights once per
+  // 8 tokens) and the prefill kernel on gate+up (37 vs 47 us).  Above 16 tokens it is
+  // within 5 % of the split prefill kernel, which keeps that range.
+  if (path == AWQ_PATH_AUTO && M > 8 && M <= 16 &&
+      awq::ts_supported(x, ldx, qweight, qzeros, scales, M, N, K, group_size)) {
+    const int s = awq::ts_splits(M, N, K, d->num_sms);
+    const bool ws_ok = s == 1 || (workspace && aligned16(workspace) &&
+                                  workspace_bytes >= awq::ts_workspace_bytes(M, N, K, d->num_sms));
+    if (ws_ok) path = AWQ_PATH_TS;
+  }
+  if (path == AWQ_PATH_TS) {
+    if (!awq::ts_supported(x, ldx, qweight, qzeros, scales, M, N, K, group_size))
+      return fail(AWQ_ERR_UNSUPPORTED, "small-M tcgen05 path cannot run M=%lld N=%lld K=%lld gs=%lld with these pointers",
+                  (long long)M, (long long)N, (long long)K, (long long)group_size);
+    const char* why = nullptr;
+    cudaError_t e = awq::launch_gemm_ts(x, ldx, qweight, qzeros, scales, out, ldo, (int)M, (int)N,
+                                        (int)K, (int)group_size, d->num_sms, d->status, st, &why,
+                                        bias, workspace, workspace_bytes);
+    if (why) return fail(AWQ_ERR_UNSUPPORTED, "small-M tcgen05 path: %s", why);
+    if (e != cudaSuccess) return fail_cuda(e, "small-M tcgen05 GEMM launch");
+    return AWQ_OK;
+  }
 
   bool use_tc = false;
   if (path == AWQ_PATH_TC) {

@@ -290,6 +290,289 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 }
 
 // ---------------------------------------------------------------------------------
+// Small-M kernel (M <= 64): the dequantized weights are the TMEM operand.
+//
+// out^T = W^T x^T: the tensor core's M dimension is 128 output columns (TMEM lanes),
+// its N dimension the NT tokens of the tile, so the MMA work shrinks with the token
+// count.  The dequant warps write W straight into tensor memory with tcgen05.st, so the
+// dequantized tile never passes through shared memory.  Per CTA: 256 columns x NT
+// tokens, K steps of 64 rows.
+//
+//   warp 0      TMA: x tile (NT x 64 fp16, 128-byte swizzle), packed weight tile (64 x 32
+//               words, 128-byte swizzle), one scale row, one zero row -> ring of TSTAGES
+//   warps 2..9  dequant into TMEM stage `as` (64 columns: two 128-lane halves x 32
+//               columns of k pairs); warp w owns lane quarter q = w % 4 and K blocks
+//               {2r, 2r+1} of the step, r = (w - 2) / 4
+//   warp 1      MMA: per step 2 halves x 4 K blocks of tcgen05.mma (M = 128, N = NT,
+//               K = 16, A from TMEM, B = x from shared memory), commits free both rings
+//   epilogue    tcgen05.ld 32x32b: thread = one output column, NT tokens
+//
+// What bounds it (measured on B200): a tcgen05.mma of this shape costs ~30 ns however
+// small N is (one of M = 128, N = 256, K = 16 costs ~71 ns), and each covers only 2048
+// weights, so the 8 MMAs of a K step take ~240 ns -- about the time HBM needs for the
+// step's 8.6 KB per SM.  With the per-step handshakes the kernel runs at ~0.5-0.7 of HBM
+// speed whatever NT is: slower than the mma.sync decode kernel up to 8 tokens, faster
+// than it (which re-reads the weights per 8 tokens) and than the prefill kernel's split
+// from 9 to 64 tokens on the shapes that need a K split (output dispatch in awq_capi.cu).
+//
+// Lane map.  In quarter q the thread (t0, t1) = (t % 4, t / 4) of a dequant warp holds
+// packed word column wc = 8 q + t1 of the tile and k rows 16 r + 4 t0 .. + 3 of each K
+// block (the tcgen05.st 16x256b fragment gives it columns 2 t0, 2 t0 + 1, i.e. those k
+// pairs).  Its 8 output slots are the 8 nibble slots u of the word: slot u goes to half
+// h = u / 4, lane 32 q + 8 (u % 4) + t1, and is element [0,2,4,6,1,3,5,7][u] of the word.
+// Lanes, halves and output columns map one to one; the epilogue inverts the map.
+constexpr int kTsAStages = 4;                    // TMEM A stages of 64 columns
+constexpr uint32_t kTsTmemCols = 512;
+constexpr uint32_t kTsDCol = kTsAStages * 64;    // accumulators: 2 halves x NT columns
+constexpr int kTsMinSteps = 4;                   // K steps per CTA at least (split-K)
+
+template <int NT>
+struct TsGeo {
+  static constexpr uint32_t X_BYTES = NT * BK * 2;
+  static constexpr uint32_t T_RAW = X_BYTES;     // 1 KB multiple (swizzle atoms)
+  static constexpr uint32_t T_SC = T_RAW + RAW_BYTES, T_ZR = T_SC + SC_BYTES;
+  static constexpr uint32_t T_STAGE = (T_ZR + ZR_BYTES + 1023) / 1024 * 1024;
+  static constexpr uint32_t TX_BYTES = X_BYTES + RAW_BYTES + SC_BYTES + ZR_BYTES;
+  static constexpr int TSTAGES = (200 * 1024) / T_STAGE < 16 ? (200 * 1024) / T_STAGE : 16;
+  static constexpr uint32_t OFF_BAR = TSTAGES * T_STAGE;
+  static constexpr uint32_t NBARS = 2 * TSTAGES + 2 * kTsAStages + 1;
+  static constexpr uint32_t OFF_MISC = OFF_BAR + NBARS * 8;
+  static constexpr uint32_t SMEM_BYTES = OFF_MISC + 16 + 1024;
+  static_assert(X_BYTES % 1024 == 0, "x tile must keep the weight tile 1 KB aligned");
+  static_assert(kTsDCol + 2 * NT <= kTsTmemCols, "TMEM columns");
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
+};
+
+template <int NT>
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_ts_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+               const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmZ,
+               const TcArgs args) {
+  using G = TsGeo<NT>;
+  constexpr int TSTAGES = G::TSTAGES, ASTAGES = kTsAStages;
+  constexpr uint32_t T_STAGE = G::T_STAGE, T_RAW = G::T_RAW, T_SC = G::T_SC, T_ZR = G::T_ZR;
+  constexpr uint32_t OFF_BAR = G::OFF_BAR, OFF_MISC = G::OFF_MISC, TX_BYTES = G::TX_BYTES;
+  constexpr uint32_t kIdescTs = sm100::idesc_f16_f32(128, NT, /*a_mn*/ 0, /*b_mn*/ 0);
+  extern __shared__ unsigned char smem_raw[];
+  const uint32_t base_raw = sm100::smem_u32(smem_raw);
+  const uint32_t sbase = (base_raw + 1023u) & ~1023u;
+  unsigned char* sgen = smem_raw + (sbase - base_raw);
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int tile_m = blockIdx.x, tile_n = blockIdx.y;
+  const int kt_all = args.K / BK;
+  const int kt0 = (int)((int64_t)blockIdx.z * kt_all / args.splits);
+  const int KT = (int)((int64_t)(blockIdx.z + 1) * kt_all / args.splits) - kt0;
+
+  auto bar_tfull = [&](int s) { return sbase + OFF_BAR + 8u * s; };
+  auto bar_tempty = [&](int s) { return sbase + OFF_BAR + 8u * (TSTAGES + s); };
+  auto bar_afull = [&](int s) { return sbase + OFF_BAR + 8u * (2 * TSTAGES + s); };
+  auto bar_aempty = [&](int s) { return sbase + OFF_BAR + 8u * (2 * TSTAGES + ASTAGES + s); };
+  const uint32_t bar_accf = sbase + OFF_BAR + 8u * (2 * TSTAGES + 2 * ASTAGES);
+  volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(sgen + OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sgen + OFF_MISC + 4);
+
+  if (tid == 0) {
+    for (int s = 0; s < TSTAGES; ++s) {
+      sm100::mbar_init(bar_tfull(s), 1);
+      sm100::mbar_init(bar_tempty(s), 1);
+    }
+    for (int s = 0; s < ASTAGES; ++s) {
+      sm100::mbar_init(bar_afull(s), kDeqWarps);
+      sm100::mbar_init(bar_aempty(s), 1);
+    }
+    sm100::mbar_init(bar_accf, 1);
+    sm100::fence_mbar_init();
+    *abort_flag = 0;
+    sm100::prefetch_tmap(&tmX);
+    sm100::prefetch_tmap(&tmW);
+    sm100::prefetch_tmap(&tmS);
+    sm100::prefetch_tmap(&tmZ);
+  }
+  if (warp == 1) {
+    sm100::tmem_alloc(sbase + OFF_MISC, kTsTmemCols);
+    sm100::tmem_relinquish();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------- TMA producer ----
+    if (lane == 0) {
+      int kt = 0;
+      for (; kt < KT; ++kt) {
+        const int s = kt % TSTAGES;
+        if (kt >= TSTAGES &&
+            !sm100::mbar_wait_bounded(bar_tempty(s), ((kt / TSTAGES) & 1) ^ 1, args.status)) {
+          *abort_flag = 1;
+          break;
+        }
+        if (*abort_flag) break;
+        const int k0 = (kt0 + kt) * BK;
+        const int grp = k0 / args.gs;
+        const uint32_t st = sbase + s * T_STAGE;
+        sm100::mbar_arrive_expect_tx(bar_tfull(s), TX_BYTES);
+        sm100::tma_load_2d(st, &tmX, bar_tfull(s), k0, tile_m * NT);
+        sm100::tma_load_2d(st + T_RAW, &tmW, bar_tfull(s), tile_n * (BN / 8), k0);
+        sm100::tma_load_2d(st + T_SC, &tmS, bar_tfull(s), tile_n * BN, grp);
+        sm100::tma_load_2d(st + T_ZR, &tmZ, bar_tfull(s), tile_n * (BN / 8), grp);
+      }
+      for (int j = (kt > TSTAGES ? kt - TSTAGES : 0); j < kt; ++j)
+        sm100::mbar_wait_bounded(bar_tfull(j % TSTAGES), (j / TSTAGES) & 1, args.status);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------- MMA issuer ------
+    if (lane == 0) {
+      for (int kt = 0; kt < KT; ++kt) {
+        const int ts = kt % TSTAGES, as = kt % ASTAGES;
+        if (!sm100::mbar_wait_bounded(bar_afull(as), (kt / ASTAGES) & 1, args.status)) {
+          *abort_flag = 1;
+          break;
+        }
+        if (*abort_flag) break;
+        sm100::tc_fence_after();
+        const uint32_t x0 = sbase + ts * T_STAGE;
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          const uint64_t bd = sm100::umma_desc_sw128(x0 + kk * 32, 16, A_SBO);
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+            sm100::umma_f16_ts(tmem + kTsDCol + h * NT, tmem + as * 64 + h * 32 + kk * 8, bd,
+                               kIdescTs, (kt | kk) != 0);
+        }
+        sm100::umma_commit(bar_tempty(ts));
+        sm100::umma_commit(bar_aempty(as));
+      }
+      sm100::umma_commit(bar_accf);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------- dequant ---------
+    const int q = warp & 3;                  // TMEM lane quarter of this warp
+    const int rb = ((warp - 2) >> 2) * 2;    // first of its two 16-row K blocks
+    const int t0 = lane & 3, t1 = lane >> 2;
+    const int wc = 8 * q + t1;               // packed word column within the tile
+    uint32_t zc[8], sc[8];
+    int grp_have = -1;
+    for (int kt = 0; kt < KT; ++kt) {
+      const int ts = kt % TSTAGES, as = kt % ASTAGES;
+      if (!sm100::mbar_wait_bounded(bar_tfull(ts), (kt / TSTAGES) & 1, args.status)) {
+        *abort_flag = 1;
+        break;
+      }
+      if (kt >= ASTAGES &&
+          !sm100::mbar_wait_bounded(bar_aempty(as), ((kt / ASTAGES) & 1) ^ 1, args.status)) {
+        *abort_flag = 1;
+        break;
+      }
+      if (*abort_flag) break;
+      sm100::tc_fence_after();
+      const unsigned char* tst = sgen + ts * T_STAGE;
+      const int grp = (kt0 + kt) * BK / args.gs;
+      if (grp != grp_have) {
+        grp_have = grp;
+        const uint32_t zw = reinterpret_cast<const uint32_t*>(tst + T_ZR)[wc];
+        const uint4 s4 = reinterpret_cast<const uint4*>(tst + T_SC)[wc];
+        const uint32_t sw[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          const uint32_t zb = __byte_perm(zw, zw, 0x1111u * (uint32_t)b);
+          zc[2 * b] = lop3_and_or(zb, kLoMask, kMagic);                              // 1024 + z
+          zc[2 * b + 1] = hmul2_u32(lop3_and_or(zb, kHiMask, kMagic), kNegInv16);    // -(64 + z)
+        }
+        // slot u holds element [0,2,4,6,1,3,5,7][u]: scale half (u / 4) of word u % 4
+#pragma unroll
+        for (int u = 0; u < 8; ++u) sc[u] = __byte_perm(sw[u & 3], sw[u & 3], u < 4 ? 0x1010u : 0x3232u);
+      }
+      const uint32_t raw = sbase + ts * T_STAGE + T_RAW;
+      uint32_t o[2][8][2];                   // [K block][slot][k pair]
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        uint32_t a[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int row = 16 * (rb + rr) + 4 * t0 + i;
+          const uint32_t addr = raw + row * 128 + ((uint32_t)((wc >> 2) ^ (row & 7)) << 4) +
+                                ((uint32_t)(wc & 3) << 2);
+          asm volatile("ld.shared.b32 %0, [%1];" : "=r"(a[i]) : "r"(addr));
+        }
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+#pragma unroll
+          for (int b = 0; b < 4; ++b) {
+            // byte b of row 2p -> bytes 0, 1; byte b of row 2p + 1 -> bytes 2, 3: the k pair
+            // (low half: row 2p) of slots 2b (low nibbles) and 2b + 1 (high nibbles)
+            const uint32_t xb = __byte_perm(a[2 * p], a[2 * p + 1], 0x4400u + 0x1111u * (uint32_t)b);
+            o[rr][2 * b][p] =
+                hmul2_u32(hsub2_u32(lop3_and_or(xb, kLoMask, kMagic), zc[2 * b]), sc[2 * b]);
+            o[rr][2 * b + 1][p] = hmul2_u32(
+                hfma2_u32(lop3_and_or(xb, kHiMask, kMagic), kInv16, zc[2 * b + 1]), sc[2 * b + 1]);
+          }
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+#pragma unroll
+        for (int lb = 0; lb < 2; ++lb) {
+          const int u0 = 4 * h + 2 * lb, u1 = u0 + 1;
+          const uint32_t r8[8] = {o[0][u0][0], o[0][u0][1], o[0][u1][0], o[0][u1][1],
+                                  o[1][u0][0], o[1][u0][1], o[1][u1][0], o[1][u1][1]};
+          const uint32_t taddr =
+              tmem + ((uint32_t)(32 * q + 16 * lb) << 16) + as * 64 + h * 32 + rb * 8;
+          sm100::tmem_st_16x256b_x2(taddr, r8);
+        }
+      }
+      sm100::tmem_st_wait();
+      sm100::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(bar_afull(as));
+    }
+
+    // ------------------------------------------------------------- epilogue --------
+    const bool ok = sm100::mbar_wait_bounded(bar_accf, 0, args.status);
+    sm100::tc_fence_after();
+    if (ok && !*abort_flag) {
+      const int h = (warp - 2) >> 2;
+      const int u = 4 * h + (lane >> 3);
+      const int e = u < 4 ? 2 * u : 2 * (u - 4) + 1;
+      const int col = tile_n * BN + 8 * (8 * q + (lane & 7)) + e;
+      const float bias = (args.bias && col < args.N) ? __half2float(args.bias[col]) : 0.f;
+#pragma unroll
+      for (int c = 0; c < NT / 16; ++c) {
+        uint32_t v[16];
+        sm100::tmem_ld_32x32b_x16(tmem + ((uint32_t)(32 * q) << 16) + kTsDCol + h * NT + c * 16, v);
+        sm100::tmem_ld_wait();
+        if (col < args.N) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int row = tile_m * NT + c * 16 + j;
+            if (row < args.M) {
+              if (args.splits > 1)
+                args.part[((size_t)blockIdx.z * args.M + row) * args.N + col] = __uint_as_float(v[j]);
+              else
+                args.out[(int64_t)row * args.ldo + col] = __float2half_rn(__uint_as_float(v[j]) + bias);
+            }
+          }
+        }
+      }
+    }
+  }
+
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    if (*abort_flag) sm100::mbar_wait_bounded(bar_accf, 0, nullptr, 100000000ull);
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, kTsTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------------
 // host: tensor maps through the driver entry point (no link-time libcuda dependency)
 // ---------------------------------------------------------------------------------
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -444,6 +727,102 @@ cudaError_t launch_gemm_tc(const void* x, int64_t ldx, const int32_t* qweight,
     gemm_tc_kernel<2><<<grid, kThreads, Geo<2>::SMEM_BYTES, stream>>>(tmA, tmW, tmS, tmZ, a);
   else
     gemm_tc_kernel<1><<<grid, kThreads, Geo<1>::SMEM_BYTES, stream>>>(tmA, tmW, tmS, tmZ, a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || a.splits == 1) return e;
+  tc_splitk_reduce<<<num_sms * 4, 256, 0, stream>>>(a.part, a.splits, M, N, a.out, ldo, a.bias);
+  return cudaGetLastError();
+}
+
+// ---- small-M kernel ---------------------------------------------------------------------
+int ts_tokens(int64_t M) { return M <= 16 ? 16 : M <= 32 ? 32 : 64; }
+
+// Split-K factor of the small-M kernel: as for the prefill kernel, but a CTA keeps at
+// least 4 K steps (its ring is deeper than that, so every copy is issued at once).
+int ts_splits(int64_t M, int64_t N, int64_t K, int num_sms) {
+  const int64_t nt = ts_tokens(M);
+  const int64_t tiles = ((M + nt - 1) / nt) * ((N + BN - 1) / BN);
+  if (tiles <= 0 || 2 * tiles >= num_sms) return 1;
+  int64_t s = num_sms / tiles;
+  if (s > K / BK / kTsMinSteps) s = K / BK / kTsMinSteps;
+  if (s > 16) s = 16;
+  return s < 1 ? 1 : (int)s;
+}
+
+size_t ts_workspace_bytes(int64_t M, int64_t N, int64_t K, int num_sms) {
+  const int s = ts_splits(M, N, K, num_sms);
+  return s > 1 ? kCounterRegionBytes + (size_t)s * M * N * sizeof(float) : 0;
+}
+
+bool ts_supported(const void* x, int64_t ldx, const int32_t* qweight, const int32_t* qzeros,
+                  const void* scales, int64_t M, int64_t N, int64_t K, int64_t group_size) {
+  return M <= 64 && tc_supported(x, ldx, qweight, qzeros, scales, M, N, K, group_size);
+}
+
+cudaError_t launch_gemm_ts(const void* x, int64_t ldx, const int32_t* qweight,
+                           const int32_t* qzeros, const void* scales, void* out, int64_t ldo,
+                           int M, int N, int K, int group_size, int num_sms, int* dev_status,
+                           cudaStream_t stream, const char** why, const void* bias,
+                           void* workspace, size_t workspace_bytes) {
+  *why = nullptr;
+  if (!ts_supported(x, ldx, qweight, qzeros, scales, M, N, K, group_size)) {
+    *why = "shape or alignment not supported";
+    return cudaSuccess;
+  }
+  if (ldo < N) {
+    *why = "ldo must be at least N";
+    return cudaSuccess;
+  }
+  const int nt = ts_tokens(M);
+  CUtensorMap tmX, tmW, tmS, tmZ;
+  const int G = K / group_size;
+  bool ok = make_map_2d(&tmX, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, K, M, (uint64_t)ldx * 2, BK, nt,
+                        CU_TENSOR_MAP_SWIZZLE_128B) &&
+            make_map_2d(&tmW, CU_TENSOR_MAP_DATA_TYPE_INT32, qweight, N / 8, K, (uint64_t)N / 2,
+                        BN / 8, BK, CU_TENSOR_MAP_SWIZZLE_128B) &&
+            make_map_2d(&tmS, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, scales, N, G, (uint64_t)N * 2, BN, 1,
+                        CU_TENSOR_MAP_SWIZZLE_NONE) &&
+            make_map_2d(&tmZ, CU_TENSOR_MAP_DATA_TYPE_INT32, qzeros, N / 8, G, (uint64_t)N / 2,
+                        BN / 8, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (!ok) {
+    *why = "cuTensorMapEncodeTiled failed";
+    return cudaSuccess;
+  }
+  static std::once_flag attr_once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(attr_once, [] {
+    attr_err = cudaFuncSetAttribute(gemm_ts_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)TsGeo<16>::SMEM_BYTES);
+    if (attr_err == cudaSuccess)
+      attr_err = cudaFuncSetAttribute(gemm_ts_kernel<32>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)TsGeo<32>::SMEM_BYTES);
+    if (attr_err == cudaSuccess)
+      attr_err = cudaFuncSetAttribute(gemm_ts_kernel<64>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)TsGeo<64>::SMEM_BYTES);
+  });
+  if (attr_err != cudaSuccess) return attr_err;
+  TcArgs a;
+  a.out = static_cast<__half*>(out);
+  a.ldo = ldo;
+  a.M = M; a.N = N; a.K = K; a.gs = group_size;
+  a.status = dev_status;
+  a.bias = static_cast<const __half*>(bias);
+  a.splits = ts_splits(M, N, K, num_sms);
+  a.part = nullptr;
+  if (a.splits > 1) {
+    if (workspace && al16(workspace) && workspace_bytes >= ts_workspace_bytes(M, N, K, num_sms))
+      a.part = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterRegionBytes);
+    else
+      a.splits = 1;
+  }
+  dim3 grid((M + nt - 1) / nt, (N + BN - 1) / BN, a.splits);
+  if (nt == 16)
+    gemm_ts_kernel<16><<<grid, kThreads, TsGeo<16>::SMEM_BYTES, stream>>>(tmX, tmW, tmS, tmZ, a);
+  else if (nt == 32)
+    gemm_ts_kernel<32><<<grid, kThreads, TsGeo<32>::SMEM_BYTES, stream>>>(tmX, tmW, tmS, tmZ, a);
+  else
+    gemm_ts_kernel<64><<<grid, kThreads, TsGeo<64>::SMEM_BYTES, stream>>>(tmX, tmW, tmS, tmZ, a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || a.splits == 1) return e;
   tc_splitk_reduce<<<num_sms * 4, 256, 0, stream>>>(a.part, a.splits, M, N, a.out, ldo, a.bias);

@@ -7,8 +7,9 @@ directory first on ``sys.path`` (``import kernels.awq_gemm``) or assign
 
 * ``awq_gemm_forward(x, qweight, qzeros, scales, group_size=128)`` -- reference
   ``kernels/awq_gemm.py:237-284``.  Same signature, same packed layout, same output
-  shape ``x.shape[:-1] + (N,)`` with ``N = scales.shape[1]``.  M <= 16 runs the
-  sm_100a decode kernel (mma.sync, split-K); larger M runs the tcgen05/TMEM prefill
+  shape ``x.shape[:-1] + (N,)`` with ``N = scales.shape[1]``.  M <= 8 runs the
+  sm_100a decode kernel (mma.sync, split-K), 9 <= M <= 16 the small-M tcgen05 kernel
+  (weights dequantized into tensor memory); larger M runs the tcgen05/TMEM prefill
   GEMM (split along K when its output tiles cannot fill the GPU) where its CTAs fill at
   least half the GPU or M > 64 (otherwise the decode kernel in 16-token launches).  Differences: inputs are validated up front (TypeError / ValueError), a CPU
   tensor raises instead of running, and no global K*N fp16 buffer is kept.
