@@ -111,6 +111,25 @@ AWQ_API int awq_gemm_f16_bias(const void* x, int64_t ldx, const int32_t* qweight
                               void* stream);
 
 /*
+ * out = silu(G) * U for the fused gate+up product P = x @ W (W = [gate | up], N
+ * columns): G = P[:, :N/2], U = P[:, N/2:], out fp16 [M, N/2] (ldo >= N/2).  Replaces the
+ * reference MLP's awq_gemm_forward + two .contiguous() slices + silu_mul_forward
+ * (model/qwen2.py:181-194, kernels/silu_mul.py:41-64): fp16-rounded G and U, fp32
+ * x * sigmoid(x) * y, one fp16 rounding.  Up to 8 tokens with N/2 a multiple of 256 the
+ * decode kernel pairs each gate strip with its up strip in its epilogue (P is never
+ * written); otherwise the product goes to a temporary inside the workspace and one
+ * elementwise kernel follows.  Workspace: awq_gemm_silu_mul_workspace_bytes bytes,
+ * zero-filled once (awq_workspace_init), the same buffer the other calls use.
+ */
+AWQ_API size_t awq_gemm_silu_mul_workspace_bytes(int64_t M, int64_t N, int64_t K,
+                                                 int64_t group_size);
+AWQ_API int awq_gemm_f16_silu_mul(const void* x, int64_t ldx, const int32_t* qweight,
+                                  const int32_t* qzeros, const void* scales, void* out,
+                                  int64_t ldo, int64_t M, int64_t N, int64_t K,
+                                  int64_t group_size, void* workspace, size_t workspace_bytes,
+                                  void* stream);
+
+/*
  * awq_gemm_f16 for callers that cannot allocate device memory: same inputs and
  * output, no workspace argument.  No counterpart in the reference (its M<=4 path
  * allocates a global K*N buffer, kernels/awq_gemm.py:255-262).  Meant for hosts that

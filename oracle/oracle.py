@@ -16,6 +16,9 @@ Everything here restates songqiuyu/Qwen2-7B-Triton_Engine:
 * ``awq_gemm_f32`` -- the reference's dequantize-then-matmul path
   (``test/compare_benchmark.py:94``, ``kernels/awq_gemm.py:266``) with the
   matmul in fp32 on the host: ``x.float() @ W.float()``.
+* ``awq_silu_mul_f32`` -- the reference MLP's activation on the fused gate+up product
+  (``model/qwen2.py:181-194``: halves sliced out of the product, then
+  ``kernels/silu_mul.py:41-64``: ``x * sigmoid(x) * y``), all in fp32.
 * ``awq_pack`` -- the inverse packing, used to build synthetic checkpoints in
   the layout ``model/qwen2.py:34-36`` registers (qweight int32 [K, N/8],
   qzeros int32 [K/gs, N/8], scales fp16 [K/gs, N]).
@@ -97,6 +100,14 @@ def awq_gemm_f32(x: np.ndarray, qweight, qzeros, scales, group_size: int = 128) 
     x2 = x.reshape(-1, x.shape[-1]).astype(np.float32)
     out = x2 @ W.astype(np.float32)
     return out.reshape(*x.shape[:-1], W.shape[1])
+
+
+def awq_silu_mul_f32(x: np.ndarray, qweight, qzeros, scales, group_size: int = 128) -> np.ndarray:
+    """fp32 [..., N/2] = silu(P[..., :N/2]) * P[..., N/2:] with P = awq_gemm_f32(x, W)."""
+    p = awq_gemm_f32(x, qweight, qzeros, scales, group_size).astype(np.float64)
+    half = p.shape[-1] // 2
+    g, u = p[..., :half], p[..., half:]
+    return (g / (1.0 + np.exp(-g)) * u).astype(np.float32)
 
 
 def max_rel_err(out: np.ndarray, ref: np.ndarray) -> float:

@@ -22,7 +22,7 @@ from . import _lib
 from ._lib import (AWQ_PATH_AUTO, AWQ_PATH_DECODE, AWQ_PATH_TC, AWQ_PATH_TS, AwqError,  # noqa: F401
                    LIB_PATH)
 
-__all__ = ["dequant", "gemm", "gemm_allreduce", "TPComm", "device_status", "workspace_for", "AwqError",
+__all__ = ["dequant", "gemm", "gemm_silu_mul", "gemm_allreduce", "TPComm", "device_status", "workspace_for", "AwqError",
            "AWQ_PATH_AUTO", "AWQ_PATH_DECODE", "AWQ_PATH_TC", "AWQ_PATH_TS", "LIB_PATH"]
 
 _ws_lock = threading.Lock()
@@ -120,7 +120,7 @@ def workspace_for(device: torch.device, nbytes: int, stream=None) -> torch.Tenso
 # a decode step issues 112 calls on the same weight tensors.
 _checked_lock = threading.Lock()
 _checked: dict = {}        # weight metadata -> (K, N) of dense, 16-byte aligned weights
-_ws_need: dict = {}        # (device, M, N, K, group_size) -> workspace bytes
+_ws_need: dict = {}        # (device, M, N, K, group_size, silu_mul) -> workspace bytes
 
 
 def _prepared_weights(qweight, qzeros, scales, group_size):
@@ -147,11 +147,13 @@ def _prepared_weights(qweight, qzeros, scales, group_size):
     return (K, N, *dense)
 
 
-def _workspace_need(lib, dev: torch.device, M: int, N: int, K: int, group_size: int) -> int:
-    key = (dev.index, M, N, K, group_size)
+def _workspace_need(lib, dev: torch.device, M: int, N: int, K: int, group_size: int,
+                    silu_mul: bool = False) -> int:
+    key = (dev.index, M, N, K, group_size, silu_mul)
     need = _ws_need.get(key)
     if need is None:
-        need = int(lib.awq_gemm_workspace_bytes(M, N, K, group_size))
+        fn = lib.awq_gemm_silu_mul_workspace_bytes if silu_mul else lib.awq_gemm_workspace_bytes
+        need = int(fn(M, N, K, group_size))
         with _checked_lock:
             if len(_ws_need) > 65536:
                 _ws_need.clear()
@@ -229,6 +231,46 @@ def gemm(x2d: torch.Tensor, qweight: torch.Tensor, qzeros: torch.Tensor, scales:
                 scales.data_ptr(), bias.data_ptr(), out.data_ptr(), out.stride(0), M, N, K, gs,
                 ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
                 stream.cuda_stream))
+    return out
+
+
+def gemm_silu_mul(x2d: torch.Tensor, qweight: torch.Tensor, qzeros: torch.Tensor,
+                  scales: torch.Tensor, group_size: int = 128,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """fp16 [M, N/2] = silu(P[:, :N/2]) * P[:, N/2:] for the fused gate+up product
+    P = x2d @ W (``awq_gemm_f16_silu_mul``): P's halves rounded to fp16, fp32
+    x * sigmoid(x) * y, one fp16 rounding -- the reference MLP's awq_gemm_forward, slices
+    and silu_mul_forward (model/qwen2.py:181-194) in one call."""
+    K, N, qweight, qzeros, scales = _prepared_weights(qweight, qzeros, scales, group_size)
+    if N % 2:
+        raise ValueError(f"N={N} is not even: no gate / up halves")
+    _require_cuda(x2d, "x")
+    if x2d.dtype != torch.float16:
+        raise TypeError(f"x must be float16, got {x2d.dtype}")
+    if x2d.dim() != 2 or x2d.shape[1] != K:
+        raise ValueError(f"x must be [M, K={K}], got {tuple(x2d.shape)}")
+    dev = x2d.device
+    if dev != qweight.device:
+        raise ValueError("x and the weights must be on one device")
+    M = x2d.shape[0]
+    if out is None:
+        out = torch.empty((M, N // 2), dtype=torch.float16, device=dev)
+    if M == 0:
+        return out
+    if x2d.stride(1) != 1 or x2d.data_ptr() % 16 or (x2d.stride(0) * 2) % 16:
+        x2d = x2d.contiguous()
+        if x2d.data_ptr() % 16:
+            x2d = x2d.clone()
+    lib = _lib.load()
+    gs = int(group_size)
+    with _DeviceGuard(dev):
+        stream = torch.cuda.current_stream(dev)
+        need = _workspace_need(lib, dev, M, N, K, gs, silu_mul=True)
+        ws = workspace_for(dev, need, stream)
+        _lib.check(lib.awq_gemm_f16_silu_mul(
+            x2d.data_ptr(), x2d.stride(0), qweight.data_ptr(), qzeros.data_ptr(),
+            scales.data_ptr(), out.data_ptr(), out.stride(0), M, N, K, gs, ws.data_ptr(),
+            ws.numel(), stream.cuda_stream))
     return out
 
 

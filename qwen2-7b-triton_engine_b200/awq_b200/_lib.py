@@ -51,6 +51,9 @@ SIGNATURES = {
     "awq_allreduce_supported": ([_P, _P, _I64, _P, _I64, _I64, _I64, _I64], _INT),
     "awq_gemm_f16_allreduce": ([_P, _P, _I64, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P,
                                 _SZ, _P], _INT),
+    "awq_gemm_silu_mul_workspace_bytes": ([_I64, _I64, _I64, _I64], _SZ),
+    "awq_gemm_f16_silu_mul": ([_P, _I64, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _SZ,
+                               _P], _INT),
 }
 
 AWQ_IPC_HANDLE_BYTES = 64

@@ -39,6 +39,12 @@ def _default_gemm_bias():
     return awq_gemm_bias_forward
 
 
+def _default_silu_mul():
+    """The library's gate+up product with silu(gate) * up in the same call."""
+    from kernels.awq_gemm import awq_gemm_silu_mul_forward
+    return awq_gemm_silu_mul_forward
+
+
 def even_split(total: int, parts: int, rank: int) -> tuple[int, int]:
     """[lo, hi) of `rank` when `total` units are dealt as evenly as possible."""
     base, extra = divmod(total, parts)
@@ -209,8 +215,15 @@ class TensorParallelMLP:
         self.inter_local = self.gate_up.parts_local[0]
         self.down = RowParallelAWQ(down, world, rank, group=group, gemm=gemm, comm=comm)
         assert (self.down.k1 - self.down.k0) == self.inter_local
+        # the library computes silu(gate) * up with the product; a substituted product
+        # (host-logic tests) goes through the slices below
+        self.silu_mul = _default_silu_mul() if gemm is None and gate_up.bias is None else None
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        if self.silu_mul is not None and self.inter_local > 0:
+            w = self.gate_up.w
+            h = self.silu_mul(x, w.qweight, w.qzeros, w.scales, w.group_size)
+            return self.down(h)
         gu = self.gate_up(x)
         gate, up = gu[..., :self.inter_local], gu[..., self.inter_local:]
         h = (F.silu(gate.float()) * up.float()).to(torch.float16)

@@ -295,6 +295,78 @@ int awq_gemm_f16_bias(const void* x, int64_t ldx, const int32_t* qweight, const 
                    workspace_bytes, stream, AWQ_PATH_AUTO, bias);
 }
 
+// ---- gate+up product followed by SiLU-mul --------------------------------------------
+// The fused decode plan (pair epilogue) when the shape allows it; the TMA kernel's pointer
+// rules are checked separately, by the caller that has the pointers.
+static bool silu_fused_plan(int64_t M, int64_t N, int64_t K, int64_t group_size, int num_sms,
+                            awq::GemvTmaPlan* p) {
+  return M >= 1 && M <= 8 && awq::plan_gemv_tma(M, N, K, group_size, num_sms, p) &&
+         awq::gemv_tma_silu_ok(*p, N);
+}
+
+// Offset of the unfused path's fp16 [M, N] product inside the workspace: after the
+// product's own workspace and never inside the counter region the other calls share.
+static size_t silu_temp_offset(int64_t M, int64_t N, int64_t K, int64_t group_size) {
+  size_t off = awq_gemm_workspace_bytes(M, N, K, group_size);
+  off = (off + 255) / 256 * 256;
+  return off < awq::kCounterRegionBytes ? awq::kCounterRegionBytes : off;
+}
+
+size_t awq_gemm_silu_mul_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t group_size) {
+  DeviceInfo* d = nullptr;
+  if (device_info(&d) || M <= 0 || N <= 0 || K <= 0) return 0;
+  size_t need = silu_temp_offset(M, N, K, group_size) + (size_t)M * N * 2;
+  awq::GemvTmaPlan p;
+  if (silu_fused_plan(M, N, K, group_size, d->num_sms, &p)) {
+    const size_t fused = awq::gemv_tma_silu_ws_bytes(p);
+    if (fused > need) need = fused;
+  }
+  return need;
+}
+
+int awq_gemm_f16_silu_mul(const void* x, int64_t ldx, const int32_t* qweight,
+                          const int32_t* qzeros, const void* scales, void* out, int64_t ldo,
+                          int64_t M, int64_t N, int64_t K, int64_t group_size, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+  int rc = check_weights(qweight, qzeros, scales, K, N, group_size);
+  if (rc) return rc;
+  if (!x || !out) return fail(AWQ_ERR_INVALID_ARG, "null x or out");
+  if (M <= 0 || M > (int64_t)1 << 30) return fail(AWQ_ERR_INVALID_ARG, "M=%lld out of range", (long long)M);
+  if (N % 2) return fail(AWQ_ERR_INVALID_ARG, "N=%lld is not even (gate and up halves)", (long long)N);
+  if (ldx < K || ldo < N / 2) return fail(AWQ_ERR_INVALID_ARG, "ldx < K or ldo < N/2");
+  if ((reinterpret_cast<uintptr_t>(x) & 1) || (reinterpret_cast<uintptr_t>(out) & 1))
+    return fail(AWQ_ERR_INVALID_ARG, "x and out must be 2-byte aligned");
+  if (!workspace || !aligned16(workspace))
+    return fail(AWQ_ERR_INVALID_ARG, "a 16-byte aligned workspace is required");
+  DeviceInfo* d = nullptr;
+  if ((rc = device_info(&d))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  awq::GemvTmaPlan p;
+  if (awq::gemv_tma_supported(qweight, N, ldx, x) &&
+      silu_fused_plan(M, N, K, group_size, d->num_sms, &p)) {
+    const size_t need = awq::gemv_tma_silu_ws_bytes(p);
+    if (workspace_bytes < need)
+      return fail(AWQ_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+    cudaError_t e = awq::launch_gemv_tma(p, x, ldx, qweight, qzeros, scales, out, ldo, (int)M,
+                                         (int)N, (int)K, (int)group_size, workspace, d->status,
+                                         st, nullptr, nullptr, /*silu_mul=*/true);
+    if (e != cudaSuccess) return fail_cuda(e, "decode (TMA) kernel launch, SiLU-mul epilogue");
+    return AWQ_OK;
+  }
+  const size_t off = silu_temp_offset(M, N, K, group_size);
+  const size_t need = off + (size_t)M * N * 2;
+  if (workspace_bytes < need)
+    return fail(AWQ_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  void* prod = static_cast<char*>(workspace) + off;
+  rc = gemm_impl(x, ldx, qweight, qzeros, scales, prod, N, M, N, K, group_size, workspace, off,
+                 stream, AWQ_PATH_AUTO, nullptr);
+  if (rc) return rc;
+  cudaError_t e = awq::launch_silu_mul(prod, N, (int)M, (int)(N / 2), out, ldo, d->num_sms, st);
+  if (e != cudaSuccess) return fail_cuda(e, "SiLU-mul kernel launch");
+  return AWQ_OK;
+}
+
 int awq_gemm_f16(const void* x, int64_t ldx, const int32_t* qweight, const int32_t* qzeros,
                  const void* scales, void* out, int64_t ldo, int64_t M, int64_t N, int64_t K,
                  int64_t group_size, void* workspace, size_t workspace_bytes, void* stream) {

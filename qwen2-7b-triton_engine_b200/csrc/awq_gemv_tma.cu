@@ -102,6 +102,13 @@ struct TmaGemvArgs {
   int* status;
   ArArgs ar;       // fused all-reduce across tensor-parallel ranks (ar.world == 1: none)
   const __half* bias;   // fp16 [N] added to every output row in fp32, or null
+  // SiLU-mul epilogue (pair_strips > 0): columns [0, N/2) are gate, [N/2, N) up, and
+  // out[m, n] = silu(gate[m, n]) * up[m, n] for n < N/2.  Strip s < pair_strips pairs
+  // with strip s + pair_strips; each tile parks its final fp32 values in pair_vals and
+  // the second tile of a pair to finish (ticket on pair_cnt) writes the product.
+  int pair_strips;
+  float* pair_vals;     // [tiles][MP][256] fp32
+  int* pair_cnt;        // [token chunks x pair_strips], zero between calls
 };
 
 __device__ __forceinline__ void mma_16816(float c[4], uint32_t a0, uint32_t a1, uint32_t a2,
@@ -521,7 +528,9 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
     return __float2half_rn(v);
   };
   auto emit = [&](int idx, int m, int n, float v) {
-    if (!ar) {
+    if (a.pair_strips > 0) {                           // parked for the SiLU-mul pair step
+      a.pair_vals[(size_t)tile * slot_stride + idx] = a.bias ? v + __half2float(a.bias[n]) : v;
+    } else if (!ar) {
       a.out[(int64_t)(m0 + m) * a.ldo + n] = out_value(n, v);
     } else {
       const size_t off = ar_tile + (size_t)a.ar.rank * ar_rank_stride + idx;
@@ -572,6 +581,33 @@ gemv_tma_kernel(const __grid_constant__ CUtensorMap tmW, const TmaGemvArgs a) {
       emit(idx, m, n, v);
     }
     if (tid == 0) a.cnt[tile] = 0;                     // ready for the next call
+  }
+  if (a.pair_strips > 0) {
+    // ---- SiLU-mul pair step (same ticket protocol as split-K): the gate and up tiles of
+    // one output strip are both final; the second to arrive rounds each to fp16, as the
+    // product's output is rounded, and writes fp16(silu(g) * u) -------------------------
+    const int s = strip, chunk_i = tile / a.strips;
+    const bool up = s >= a.pair_strips;
+    const int ps = up ? s - a.pair_strips : s;
+    const int pid = chunk_i * a.pair_strips + ps;
+    const int partner = chunk_i * a.strips + (up ? ps : ps + a.pair_strips);
+    __syncthreads();
+    if (tid == 0) *last_flag = (atom_add_acq_rel_gpu(a.pair_cnt + pid, 1) == 1) ? 1 : 0;
+    __syncthreads();
+    if (!*last_flag) return;
+    const float* gv = a.pair_vals + (size_t)(up ? partner : tile) * slot_stride;
+    const float* uv = a.pair_vals + (size_t)(up ? tile : partner) * slot_stride;
+    const int nh = a.N / 2;
+    for (int idx = tid; idx < Mc * kStripN; idx += kThreads) {
+      const int m = idx / kStripN, nl = idx - m * kStripN;
+      const int n = ps * kStripN + nl;
+      if (n >= nh) continue;
+      const float gg = __half2float(__float2half_rn(__ldcg(gv + idx)));
+      const float uu = __half2float(__float2half_rn(__ldcg(uv + idx)));
+      a.out[(int64_t)(m0 + m) * a.ldo + n] = __float2half_rn(gg * (1.0f / (1.0f + expf(-gg))) * uu);
+    }
+    if (tid == 0) a.pair_cnt[pid] = 0;
+    return;
   }
   if (!ar) return;
 
@@ -727,6 +763,20 @@ bool plan_gemv_tma(int64_t M, int64_t N, int64_t K, int64_t gs, int num_sms, Gem
   }
 }
 
+// SiLU-mul epilogue: the gate and up halves must split at a strip boundary, and the tile
+// and pair counters must fit the counter region.
+bool gemv_tma_silu_ok(const GemvTmaPlan& p, int64_t N) {
+  return N % (2 * kStripN) == 0 && p.strips % 2 == 0 &&
+         (int64_t)p.tiles + p.tiles / 2 <= kMaxCounters;
+}
+size_t silu_vals_offset(const GemvTmaPlan& p) {
+  return p.ws_bytes > 0 ? p.ws_bytes : kCounterRegionBytes;
+}
+size_t gemv_tma_silu_ws_bytes(const GemvTmaPlan& p) {
+  const size_t mp = 4 * (size_t)p.toksets;
+  return silu_vals_offset(p) + (size_t)p.tiles * mp * kStripN * sizeof(float);
+}
+
 bool gemv_tma_supported(const int32_t* qweight, int64_t N, int64_t ldx, const void* x) {
   return (N % 32 == 0) && ((reinterpret_cast<uintptr_t>(qweight) & 15) == 0) &&
          ((reinterpret_cast<uintptr_t>(x) & 15) == 0) && (ldx % 8 == 0) && encode_fn() != nullptr;
@@ -736,10 +786,11 @@ cudaError_t launch_gemv_tma(const GemvTmaPlan& p, const void* x, int64_t ldx,
                             const int32_t* qweight, const int32_t* qzeros, const void* scales,
                             void* out, int64_t ldo, int M, int N, int K, int group_size,
                             void* workspace, int* dev_status, cudaStream_t stream,
-                            const ArArgs* ar, const void* bias) {
+                            const ArArgs* ar, const void* bias, bool silu_mul) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return cudaErrorNotSupported;
-  if (p.ws_bytes > 0 && !workspace) return cudaErrorInvalidValue;
+  if ((p.ws_bytes > 0 || silu_mul) && !workspace) return cudaErrorInvalidValue;
+  if (silu_mul && (!gemv_tma_silu_ok(p, N) || (ar && ar->world > 1))) return cudaErrorInvalidValue;
   CUtensorMap tm;
   cuuint64_t dims[2] = {(cuuint64_t)(N / 8), (cuuint64_t)K};
   cuuint64_t strides[1] = {(cuuint64_t)N / 2};
@@ -771,6 +822,18 @@ cudaError_t launch_gemv_tma(const GemvTmaPlan& p, const void* x, int64_t ldx,
   a.l2pf = pdl_enabled() ? kL2PrefetchStages : 0;
   a.status = dev_status;
   a.bias = static_cast<const __half*>(bias);
+  a.pair_strips = 0;
+  a.pair_vals = nullptr;
+  a.pair_cnt = nullptr;
+  if (silu_mul) {
+    // counters: split-K per tile at [0, tiles), pairs after them; values after the
+    // split-K slots
+    a.cnt = static_cast<int*>(workspace);
+    a.pair_strips = p.strips / 2;
+    a.pair_cnt = static_cast<int*>(workspace) + p.tiles;
+    a.pair_vals = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) +
+                                           silu_vals_offset(p));
+  }
   if (ar) {
     a.ar = *ar;
   } else {

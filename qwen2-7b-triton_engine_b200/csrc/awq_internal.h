@@ -85,11 +85,23 @@ struct ArArgs {
   int* state;                  // this rank's state words
   unsigned long long timeout_ns;
 };
+// silu_mul: out is [M, N/2] = silu(columns [0, N/2)) * columns [N/2, N) of the product,
+// computed in the kernel's epilogue (needs gemv_tma_silu_ok and gemv_tma_silu_ws_bytes of
+// workspace, zero-initialised counters included).
 cudaError_t launch_gemv_tma(const GemvTmaPlan& plan, const void* x, int64_t ldx,
                             const int32_t* qweight, const int32_t* qzeros, const void* scales,
                             void* out, int64_t ldo, int M, int N, int K, int group_size,
                             void* workspace, int* dev_status, cudaStream_t stream,
-                            const ArArgs* ar = nullptr, const void* bias = nullptr);
+                            const ArArgs* ar = nullptr, const void* bias = nullptr,
+                            bool silu_mul = false);
+bool gemv_tma_silu_ok(const GemvTmaPlan& plan, int64_t N);
+size_t gemv_tma_silu_ws_bytes(const GemvTmaPlan& plan);
+
+// ---- SiLU-mul of a [M, 2I] fp16 product (awq_silu.cu) ---------------------------------
+// out[m, n] = fp16(silu(gu[m, n]) * gu[m, I + n]), fp32 math (the reference's
+// kernels/silu_mul.py:41-64 on the two halves of model/qwen2.py:183-188).
+cudaError_t launch_silu_mul(const void* gu, int64_t ldg, int M, int I, void* out, int64_t ldo,
+                            int num_sms, cudaStream_t stream);
 constexpr size_t kGemvTmaMaxSmem = 227 * 1024;   // sm_100's opt-in per-block maximum
 
 // ---- prefill GEMM on tcgen05 / TMEM (awq_gemm_tc.cu) ----------------------------------

@@ -16,6 +16,11 @@ directory first on ``sys.path`` (``import kernels.awq_gemm``) or assign
 * ``awq_gemm_bias_forward(x, qweight, qzeros, scales, bias, group_size=128)`` -- not in
   the reference: the product plus the layer's bias in one kernel, for the callers that
   add the bias afterwards (``model/qwen2.py:45-46,108-109``).
+* ``awq_gemm_silu_mul_forward(x, qweight, qzeros, scales, group_size=128)`` -- not in the
+  reference: silu(gate) * up of the fused gate+up product in one call, replacing
+  ``awq_gemm_forward`` + the two ``.contiguous()`` slices + ``silu_mul_forward`` of the
+  reference MLP (``model/qwen2.py:181-194``, ``kernels/silu_mul.py:41-64``).  Output
+  ``x.shape[:-1] + (N/2,)``.
 * ``_dequant_to_fp16(qweight, qzeros, scales, out_buf, group_size=128)`` --
   reference ``kernels/awq_gemm.py:66-87``; writes the bit-identical fp16 weights.
 """
@@ -25,7 +30,8 @@ import torch
 
 import awq_b200
 
-__all__ = ["awq_gemm_forward", "awq_gemm_bias_forward", "_dequant_to_fp16"]
+__all__ = ["awq_gemm_forward", "awq_gemm_bias_forward", "awq_gemm_silu_mul_forward",
+           "_dequant_to_fp16"]
 
 
 def _dequant_to_fp16(qweight: torch.Tensor, qzeros: torch.Tensor, scales: torch.Tensor,
@@ -67,3 +73,19 @@ def awq_gemm_bias_forward(x: torch.Tensor, qweight: torch.Tensor, qzeros: torch.
     N = scales.shape[1]
     out = awq_b200.gemm(x_flat, qweight, qzeros, scales, group_size, bias=bias)
     return out.view(*in_shape[:-1], N)
+
+
+def awq_gemm_silu_mul_forward(x: torch.Tensor, qweight: torch.Tensor, qzeros: torch.Tensor,
+                              scales: torch.Tensor, group_size: int = 128) -> torch.Tensor:
+    """``silu(P[..., :N/2]) * P[..., N/2:]`` for ``P = awq_gemm_forward(x, ...)`` with the
+    fused gate+up weights (N = 2 * intermediate): the MLP activation of the reference
+    (``model/qwen2.py:181-194``) in one call; up to 8 tokens P is never written."""
+    if not isinstance(x, torch.Tensor):
+        raise TypeError("x must be a torch.Tensor")
+    if x.dim() < 1:
+        raise ValueError("x must have at least one dimension")
+    in_shape = x.shape
+    x_flat = x.reshape(-1, x.shape[-1])
+    N = scales.shape[1]
+    out = awq_b200.gemm_silu_mul(x_flat, qweight, qzeros, scales, group_size)
+    return out.view(*in_shape[:-1], N // 2)
