@@ -498,7 +498,8 @@ def decode_sweep(torch, lib, awq_b200, dev, hbm_peak):
             us = e0.elapsed_time(e1) * 1e3 / (nrep * copies)
             gbs = alg_bytes(M, K, N) / (us * 1e-6) / 1e9
             out[f"{name}_M{M}"] = {"us": round(us, 2), "GBps": round(gbs, 1),
-                                   "frac": round(gbs / hbm_peak, 3)}
+                                   "frac": round(gbs / hbm_peak, 3),
+                                   "kernel": "decode" if M <= 8 else "tcgen05-small"}
             del g
         del pool
     return out
@@ -562,7 +563,8 @@ def run_reference(args):
 
 def run_case(args):
     """One kernel on one shape, `--reps` launches (for ncu captures):
-    --case decode:<shape>:<M> | prefill:<shape>:<M> | dequant:<shape>, shapes from SWEEP."""
+    --case decode:<shape>:<M> | prefill:<shape>:<M> | small:<shape>:<M> (tcgen05 small-M
+    kernel) | silu:<shape>:<M> (product + SiLU-mul) | dequant:<shape>, shapes from SWEEP."""
     import torch
 
     import awq_b200
@@ -575,11 +577,18 @@ def run_case(args):
         out = torch.empty((K, N), dtype=torch.float16, device=dev)
         for _ in range(args.reps):
             awq_b200.dequant(qw, qz, s, GS, out=out)
+    elif kind == "silu":
+        M = int(rest[0]) if rest else 1
+        x = torch.randn((M, K), device=dev, generator=gen).half()
+        out = torch.empty((M, N // 2), dtype=torch.float16, device=dev)
+        for _ in range(args.reps):
+            awq_b200.gemm_silu_mul(x, qw, qz, s, GS, out=out)
     else:
-        M = int(rest[0]) if rest else (1 if kind == "decode" else 2048)
+        M = int(rest[0]) if rest else {"decode": 1, "small": 16}.get(kind, 2048)
         x = torch.randn((M, K), device=dev, generator=gen).half()
         out = torch.empty((M, N), dtype=torch.float16, device=dev)
-        path = awq_b200.AWQ_PATH_DECODE if kind == "decode" else awq_b200.AWQ_PATH_TC
+        path = {"decode": awq_b200.AWQ_PATH_DECODE, "small": awq_b200.AWQ_PATH_TS,
+                "prefill": awq_b200.AWQ_PATH_TC}[kind]
         for _ in range(args.reps):
             awq_b200.gemm(x, qw, qz, s, GS, path=path, out=out)
     torch.cuda.synchronize()
