@@ -16,6 +16,9 @@ Everything here restates songqiuyu/Qwen2-7B-Triton_Engine:
 * ``awq_gemm_f32`` -- the reference's dequantize-then-matmul path
   (``test/compare_benchmark.py:94``, ``kernels/awq_gemm.py:266``) with the
   matmul in fp32 on the host: ``x.float() @ W.float()``.
+* ``silu_mul_f16`` -- ``kernels/silu_mul.py:31-38`` (fp16 in, fp32 x * sigmoid(x) * y,
+  fp16 out); pinned bit-exact against the reference's interpreted kernel
+  (``tests/golden/silu_golden.npz``, made by ``tests/golden/make_golden_silu.py``).
 * ``awq_silu_mul_f32`` -- the reference MLP's activation on the fused gate+up product
   (``model/qwen2.py:181-194``: halves sliced out of the product, then
   ``kernels/silu_mul.py:41-64``: ``x * sigmoid(x) * y``), all in fp32.
@@ -100,6 +103,16 @@ def awq_gemm_f32(x: np.ndarray, qweight, qzeros, scales, group_size: int = 128) 
     x2 = x.reshape(-1, x.shape[-1]).astype(np.float32)
     out = x2 @ W.astype(np.float32)
     return out.reshape(*x.shape[:-1], W.shape[1])
+
+
+def silu_mul_f16(gate: np.ndarray, up: np.ndarray) -> np.ndarray:
+    """fp16 silu(gate) * up with fp32 arithmetic (kernels/silu_mul.py:31-38: load as fp32,
+    x * sigmoid(x) * y, store fp16)."""
+    with np.errstate(over="ignore"):
+        x = np.asarray(gate, dtype=np.float16).astype(np.float32)
+        y = np.asarray(up, dtype=np.float16).astype(np.float32)
+        sig = np.float32(1.0) / (np.float32(1.0) + np.exp(-x))
+        return (x * sig * y).astype(np.float16)
 
 
 def awq_silu_mul_f32(x: np.ndarray, qweight, qzeros, scales, group_size: int = 128) -> np.ndarray:

@@ -14,6 +14,7 @@ for p in (str(REPO), str(PKG)):
         sys.path.insert(0, p)
 
 GOLDEN = REPO / "tests" / "golden" / "awq_golden.npz"
+SILU_GOLDEN = REPO / "tests" / "golden" / "silu_golden.npz"
 
 
 def pytest_configure(config):
@@ -44,3 +45,14 @@ def cuda():
     torch.backends.cuda.matmul.allow_tf32 = False
     torch.backends.cudnn.allow_tf32 = False
     return torch.device("cuda", 0)
+
+
+@pytest.fixture(scope="session")
+def silu_golden():
+    """Cases of tests/golden/make_golden_silu.py: name -> {array name: array}."""
+    data = np.load(SILU_GOLDEN, allow_pickle=False)
+    cases = {}
+    for key in data.files:
+        name, field = key.split("/", 1)
+        cases.setdefault(name, {})[field] = data[key]
+    return cases

@@ -110,3 +110,18 @@ def test_silu_mul_small_halves(cuda):
         assert h.shape == (3, N // 2)
         assert O.max_rel_err(h.float().cpu().numpy(), O.awq_silu_mul_f32(x, qw, qz, s)) <= TOL
     assert awq_b200.device_status() == 0
+
+
+def test_silu_mul_golden(silu_golden, cuda):
+    """Against the reference's own MLP sequence (torch_awq_gemm product, halves, interpreted
+    _silu_mul_kernel) committed in tests/golden/silu_golden.npz: M = 3 (pair epilogue) and
+    M = 12 with halves of 320 columns (product + elementwise kernel)."""
+    import awq_b200
+    for name in ("mlp_k256_i256_m3", "mlp_k384_i320_m12"):
+        c = silu_golden[name]
+        gs = int(c["group_size"])
+        dx, dqw, dqz, ds = _dev(cuda, c["x"], c["qweight"], c["qzeros"], c["scales"])
+        h = awq_b200.gemm_silu_mul(dx, dqw, dqz, ds, gs)
+        ref = c["out_bits"].view(np.float16).astype(np.float32)
+        assert O.max_rel_err(h.float().cpu().numpy(), ref) <= TOL, name
+    assert awq_b200.device_status() == 0

@@ -92,3 +92,23 @@ def test_oracle_rejects_bad_shapes():
         O.awq_dequant(qw, qz, s, group_size=96)
     with pytest.raises(ValueError):
         O.awq_dequant(qw, qz, s[:, :32], group_size=128)
+
+
+def test_silu_mul_f16_bit_exact_vs_reference(silu_golden):
+    # the reference's _silu_mul_kernel (kernels/silu_mul.py:17-38), interpreted on the CPU,
+    # over N(0, 3), saturating, overflowing, signed-zero and subnormal inputs
+    c = silu_golden["elementwise"]
+    out = O.silu_mul_f16(c["g"], c["u"])
+    assert _same_bits(out, c["out_bits"].view(np.float16))
+
+
+def test_silu_mlp_sequence_vs_oracle(silu_golden):
+    # the reference MLP's fp16 sequence (product, halves, silu_mul) against the fp32 oracle
+    names = [n for n in silu_golden if n.startswith("mlp_")]
+    assert len(names) == 2
+    for name in names:
+        c = silu_golden[name]
+        ref = c["out_bits"].view(np.float16).astype(np.float32)
+        out = O.awq_silu_mul_f32(c["x"], c["qweight"], c["qzeros"], c["scales"], int(c["group_size"]))
+        assert out.shape == ref.shape, name
+        assert O.max_rel_err(out, ref) <= 1e-2, name
