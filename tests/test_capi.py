@@ -85,3 +85,32 @@ def test_weight_checks():
     # device error comes first and is the one a caller sees
     with pytest.raises(ValueError):
         awq_b200.check_weights(qw, qz, s, 128)
+
+
+def test_new_entry_points_reject_bad_input_without_a_device():
+    import awq_b200._lib as L
+    lib = L.load()
+    # gate+up with SiLU-mul: null weights, then a null workspace, before any CUDA call
+    rc = lib.awq_gemm_f16_silu_mul(16, 256, None, None, None, 16, 32, 1, 64, 256, 128, 16, 1 << 20,
+                                   None)
+    assert rc == L.AWQ_ERR_INVALID_ARG
+    rc = lib.awq_gemm_f16_silu_mul(16, 256, 16, 16, 16, 16, 32, 1, 64, 256, 128, None, 0, None)
+    assert rc == L.AWQ_ERR_INVALID_ARG
+    assert b"workspace" in lib.awq_last_error()
+    rc = lib.awq_gemm_f16_silu_mul(16, 256, 16, 16, 16, 16, 16, 1, 64, 256, 128, 16, 1 << 20,
+                                   None)                                  # ldo < N / 2
+    assert rc == L.AWQ_ERR_INVALID_ARG
+    # explicit small-M path: an unknown path number is refused before the device is touched
+    rc = lib.awq_gemm_f16_ex(16, 256, 16, 16, 16, 16, 64, 1, 64, 256, 128, None, 0, None, 7)
+    assert rc == L.AWQ_ERR_INVALID_ARG
+    assert L.AWQ_PATH_TS == 3
+
+
+def test_silu_dropin_refuses_cpu_tensors_and_keeps_signature():
+    import inspect
+    from kernels import awq_gemm
+    sig = inspect.signature(awq_gemm.awq_gemm_silu_mul_forward)
+    assert list(sig.parameters) == ["x", "qweight", "qzeros", "scales", "group_size"]
+    qw, qz, s = _layer(N=512)
+    with pytest.raises(ValueError, match="CUDA only"):
+        awq_gemm.awq_gemm_silu_mul_forward(torch.zeros(1, 256, dtype=torch.float16), qw, qz, s)
