@@ -1,5 +1,5 @@
-"""CPU: host logic of the tensor-parallel wrapper (awq_b200.tp) with world_size-2 `gloo`
-process groups.  The GEMM is the CPU oracle here (injected through ``gemm=``); on GPUs
+"""CPU: host logic of the tensor-parallel wrapper (awq_b200.tp) with `gloo` process groups
+of 2, 4 and 8 ranks.  The GEMM is the CPU oracle here (injected through ``gemm=``); on GPUs
 the same classes call the sm_100a library and NCCL."""
 from __future__ import annotations
 
@@ -87,8 +87,13 @@ def _worker(rank, world, port, K, inter, hidden, seed, q):
         dist.destroy_process_group()
 
 
-def test_tp_mlp_and_row_parallel_gloo_world2():
-    world, K, inter, hidden, seed = 2, 256, 512, 256, 11
+@pytest.mark.parametrize("world,inter,hidden", [
+    (2, 512, 256),
+    (4, 1024, 384),      # o has 3 groups for 4 ranks: the last rank holds no rows
+    (8, 1024, 512),      # one group of the intermediate dimension per rank
+])
+def test_tp_mlp_and_row_parallel_gloo(world, inter, hidden):
+    K, seed = hidden, 11
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
