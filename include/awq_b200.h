@@ -83,8 +83,9 @@ AWQ_API int awq_workspace_init(void* workspace, size_t workspace_bytes, void* st
 /*
  * out fp16 [M, N] (row stride ldo) = x fp16 [M, K] (row stride ldx) @ W, fp32
  * accumulation.  Replaces awq_gemm_forward (kernels/awq_gemm.py:237-284) after its
- * reshape of x to [M, K]: M <= 16 runs the decode kernel, larger M the tcgen05
- * GEMM when the shape allows it, else the decode kernel over 16-token chunks.
+ * reshape of x to [M, K]: M <= 8 runs the decode kernel, 9 <= M <= 16 the small-M
+ * tcgen05 kernel, larger M the tcgen05 prefill GEMM, each when the shape allows it,
+ * else the decode kernel over 16-token chunks (AWQ_PATH_AUTO below).
  */
 AWQ_API int awq_gemm_f16(const void* x, int64_t ldx, const int32_t* qweight, const int32_t* qzeros,
                  const void* scales, void* out, int64_t ldo, int64_t M, int64_t N, int64_t K,
