@@ -114,3 +114,36 @@ def test_silu_dropin_refuses_cpu_tensors_and_keeps_signature():
     qw, qz, s = _layer(N=512)
     with pytest.raises(ValueError, match="CUDA only"):
         awq_gemm.awq_gemm_silu_mul_forward(torch.zeros(1, 256, dtype=torch.float16), qw, qz, s)
+
+
+def test_header_is_c_and_links_from_a_c_host(tmp_path):
+    """The boundary is plain C: a C99 program includes include/awq_b200.h, links the
+    in-tree libawq_b200.so and calls entry points that need no device (version, error
+    string, argument checks), as a non-Python host would."""
+    import shutil
+    import subprocess
+
+    import awq_b200
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    src = tmp_path / "host.c"
+    src.write_text(r"""
+#include <stdio.h>
+#include "awq_b200.h"
+int main(void) {
+  int v = awq_version();
+  int rc = awq_gemm_f16(0, 256, 0, 0, 0, 0, 64, 1, 64, 256, 128, 0, 0, 0);
+  const char* e = awq_last_error();
+  int rc2 = awq_gemm_f16_silu_mul(0, 256, 0, 0, 0, 0, 32, 1, 64, 256, 128, 0, 0, 0);
+  printf("%d %d %d %s\n", v, rc == AWQ_ERR_INVALID_ARG, rc2 == AWQ_ERR_INVALID_ARG, e ? "msg" : "none");
+  return 0;
+}
+""")
+    exe = tmp_path / "host"
+    lib = awq_b200.LIB_PATH
+    subprocess.run([cc, "-std=c99", "-Wall", "-Werror", "-I", str(REPO / "include"), str(src),
+                    "-o", str(exe), "-L", str(lib.parent), "-lawq_b200",
+                    f"-Wl,-rpath,{lib.parent}"], check=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split()
+    assert int(out[0]) >= 100 and out[1:] == ["1", "1", "msg"]
