@@ -1,7 +1,9 @@
-// awq_gemm_tc.cu -- prefill AWQ W4A16 GEMM on the sm_100a tensor cores (tcgen05 + TMEM).
+// awq_gemm_tc.cu -- AWQ W4A16 GEMMs on the sm_100a tensor cores (tcgen05 + TMEM): the
+// prefill kernel (gemm_tc_kernel, below), the small-M kernel with the weights as the TMEM
+// operand (gemm_ts_kernel, further down) and the split-K reduce kernel both use.
 //
 // Replaces _awq_gemm_kernel (songqiuyu/Qwen2-7B-Triton_Engine kernels/awq_gemm.py:152-228,
-// 64x64 tiles on mma.sync) for M > 16.  One CTA computes a 128 x 256 tile of
+// 64x64 tiles on mma.sync) for M > 8.  The prefill kernel's CTA computes a 128 x 256 tile of
 // out = x @ W with fp32 accumulation in tensor memory:
 //
 //   warp 0      TMA producer: per 64-deep K step loads the x tile (128 x 64 fp16,
