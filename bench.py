@@ -12,7 +12,8 @@ step streams from HBM (no flush needed).  Weights are random int4 in the AWQ lay
 with the benchmark's distributions (synthetic data; no checkpoint exists here).
 
   value     algorithmic bytes of a step / device time of a step (CUDA events over K
-            CUDA-graph replays), TB/s, whole job (max over ranks)
+            CUDA-graph replays), TB/s, whole job (max over ranks); tokens_per_s is
+            1 / that step time (the linears' decode rate of the 28-layer stack)
   e2e       the same bytes / time of a step made through the public drop-in
             ``awq_gemm_forward`` with every call's x copied from pinned host memory
             and every output copied back inside the timed region
@@ -344,7 +345,9 @@ def run_ours(args):
         result = {
             "metric": "AWQ GEMM HBM TB/s (M=1 decode) & TFLOPS (M=2048 prefill), % of B200 roofline",
             "value": round(value, 4), "unit": "TB/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
+            "warmup": args.warmup, "ms_per_step": round(ms, 5),
+            "tokens_per_s": round(1e3 / ms, 1),      # one step = one decode token, 28 layers
+            "higher_is_better": True,
             "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f16",
             "data": "synthetic (seeded random int4 AWQ weights, x ~ N(0,1); no checkpoint)",
             "config": {"workload": "decode M=1 through the AWQ linears of the 28-layer Qwen2-7B "
@@ -401,7 +404,7 @@ def run_ours(args):
         e2e_ms = float(t.item())
     if rank == 0:
         result["e2e"] = {"value": round(full_bytes / (e2e_ms * 1e-3) / 1e12, 4), "unit": "TB/s",
-                         "ms_per_step": round(e2e_ms, 4),
+                         "ms_per_step": round(e2e_ms, 4), "tokens_per_s": round(1e3 / e2e_ms, 1),
                          "h2d_bytes_per_step": sum(2 * K for (_, K, _, _, _) in calls),
                          "d2h_bytes_per_step": sum(2 * N for (_, _, N, _, _) in calls),
                          "api": "kernels.awq_gemm.awq_gemm_forward (eager, 112 calls"
