@@ -4,6 +4,7 @@ from __future__ import annotations
 
 import numpy as np
 import pytest
+from hypothesis import given, settings, strategies as st
 
 from oracle import oracle as O
 
@@ -112,3 +113,35 @@ def test_silu_mlp_sequence_vs_oracle(silu_golden):
         out = O.awq_silu_mul_f32(c["x"], c["qweight"], c["qzeros"], c["scales"], int(c["group_size"]))
         assert out.shape == ref.shape, name
         assert O.max_rel_err(out, ref) <= 1e-2, name
+
+
+def _scalar_dequant(qweight, qzeros, scales, group_size, k, n):
+    """W[k, n] by the reference's formula, one element at a time in pure Python
+    (kernels/awq_gemm.py:36-59): nibble at shift 4 * [0,4,1,5,2,6,3,7][n % 8] of the
+    packed words, (fp16(w) - fp16(z)) * scale with one fp16 rounding per operation."""
+    shift = 4 * [0, 4, 1, 5, 2, 6, 3, 7][n % 8]
+    w = (int(qweight[k, n // 8]) >> shift) & 0xF
+    z = (int(qzeros[k // group_size, n // 8]) >> shift) & 0xF
+    d = np.float16(np.float16(w) - np.float16(z))
+    with np.errstate(over="ignore"):
+        return np.float16(d * scales[k // group_size, n])
+
+
+
+@settings(max_examples=40, deadline=None)
+@given(groups=st.integers(1, 4), gs=st.sampled_from([32, 64, 128]), words=st.integers(1, 6),
+       seed=st.integers(0, 2**32 - 1))
+def test_three_restatements_agree(groups, gs, words, seed):
+    """numpy, C and a scalar pure-Python restatement give the same bits on random shapes,
+    full-range packed words and fp16 scales of every magnitude and sign."""
+    K, N = groups * gs, 8 * words
+    rng = np.random.default_rng(seed)
+    qw = rng.integers(-2**31, 2**31, size=(K, N // 8), dtype=np.int64).astype(np.int32)
+    qz = rng.integers(-2**31, 2**31, size=(groups, N // 8), dtype=np.int64).astype(np.int32)
+    bits = rng.integers(0, 0x7C00, size=(groups, N), dtype=np.int64).astype(np.uint16)
+    sign = (rng.integers(0, 2, size=(groups, N)).astype(np.uint16) << 15).astype(np.uint16)
+    s = (bits | sign).view(np.float16)
+    a = O.awq_dequant(qw, qz, s, gs)
+    assert _same_bits(a, O.c_awq_dequant(qw, qz, s, gs))
+    for k, n in zip(rng.integers(0, K, 16), rng.integers(0, N, 16)):
+        assert _same_bits(np.array([a[k, n]]), np.array([_scalar_dequant(qw, qz, s, gs, k, n)]))
