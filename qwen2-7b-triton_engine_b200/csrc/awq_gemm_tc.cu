@@ -697,15 +697,15 @@ cudaError_t launch_gemm_tc(const void* x, int64_t ldx, const int32_t* qweight,
     *why = "cuTensorMapEncodeTiled failed";
     return cudaSuccess;
   }
-  static std::once_flag attr_once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(attr_once, [] {
-    attr_err = cudaFuncSetAttribute(gemm_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)Geo<1>::SMEM_BYTES);
-    if (attr_err == cudaSuccess)
-      attr_err = cudaFuncSetAttribute(gemm_tc_kernel<2>,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)Geo<2>::SMEM_BYTES);
+  static PerDeviceOnce attr_once;
+  const cudaError_t attr_err = attr_once.run([] {
+    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<1>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)Geo<1>::SMEM_BYTES);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gemm_tc_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)Geo<2>::SMEM_BYTES);
+    return e;
   });
   if (attr_err != cudaSuccess) return attr_err;
   TcArgs a;
@@ -789,19 +789,18 @@ cudaError_t launch_gemm_ts(const void* x, int64_t ldx, const int32_t* qweight,
     *why = "cuTensorMapEncodeTiled failed";
     return cudaSuccess;
   }
-  static std::once_flag attr_once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(attr_once, [] {
-    attr_err = cudaFuncSetAttribute(gemm_ts_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)TsGeo<16>::SMEM_BYTES);
-    if (attr_err == cudaSuccess)
-      attr_err = cudaFuncSetAttribute(gemm_ts_kernel<32>,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)TsGeo<32>::SMEM_BYTES);
-    if (attr_err == cudaSuccess)
-      attr_err = cudaFuncSetAttribute(gemm_ts_kernel<64>,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)TsGeo<64>::SMEM_BYTES);
+  static PerDeviceOnce attr_once;
+  const cudaError_t attr_err = attr_once.run([] {
+    cudaError_t e = cudaFuncSetAttribute(gemm_ts_kernel<16>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)TsGeo<16>::SMEM_BYTES);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gemm_ts_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)TsGeo<32>::SMEM_BYTES);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gemm_ts_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)TsGeo<64>::SMEM_BYTES);
+    return e;
   });
   if (attr_err != cudaSuccess) return attr_err;
   TcArgs a;

@@ -690,10 +690,9 @@ bool pdl_enabled() {
 template <int TOKSETS>
 cudaError_t launch_t(const CUtensorMap& tm, const TmaGemvArgs& a, int grid, size_t smem,
                      cudaStream_t stream) {
-  static std::once_flag once;
-  static cudaError_t attr = cudaSuccess;
-  std::call_once(once, [] {
-    attr = cudaFuncSetAttribute(gemv_tma_kernel<TOKSETS>,
+  static PerDeviceOnce attr_once;
+  const cudaError_t attr = attr_once.run([] {
+    return cudaFuncSetAttribute(gemv_tma_kernel<TOKSETS>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemvTmaMaxSmem);
   });
   if (attr != cudaSuccess) return attr;

@@ -6,7 +6,35 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <atomic>
+#include <mutex>
+
 namespace awq {
+
+// Kernel attributes set with cudaFuncSetAttribute (the dynamic shared-memory limit) belong
+// to the current device, so a process that drives several GPUs must set them on each:
+// `run(set)` calls `set` once per device for this call site and returns its result on
+// every later call on that device.
+struct PerDeviceOnce {
+  static constexpr int kDevices = 64;
+  std::atomic<uint64_t> done{0};
+  std::mutex mu;
+  cudaError_t err[kDevices] = {};
+  template <class F>
+  cudaError_t run(F&& set) {
+    int dev = 0;
+    const cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kDevices) return cudaErrorInvalidDevice;
+    if ((done.load(std::memory_order_acquire) >> dev) & 1u) return err[dev];
+    std::lock_guard<std::mutex> lk(mu);
+    if (!((done.load(std::memory_order_relaxed) >> dev) & 1u)) {
+      err[dev] = set();
+      done.fetch_or(uint64_t(1) << dev, std::memory_order_release);
+    }
+    return err[dev];
+  }
+};
 
 // ---- dequant (awq_dequant.cu) -------------------------------------------------------
 cudaError_t launch_dequant(const int32_t* qweight, const int32_t* qzeros, const void* scales,

@@ -270,3 +270,22 @@ def test_bias_epilogue(cuda, M, K, N, gs):
     assert awq_b200.device_status() == 0
     with pytest.raises(ValueError):
         awq_gemm.awq_gemm_bias_forward(dx, dqw, dqz, ds, db[:-8], gs)
+
+
+def test_two_devices_in_one_process(cuda):
+    """One process driving two GPUs: every kernel family (decode, small-M, prefill) runs
+    on both devices -- their shared-memory limits are raised per device."""
+    import awq_b200
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    K, N = 512, 512
+    qw, qz, s = O.make_awq_layer(K, N, 128, seed=31)
+    for dev_index in (1, 0, 1):
+        d = torch.device("cuda", dev_index)
+        dqw, dqz, ds = (torch.from_numpy(np.ascontiguousarray(a)).to(d) for a in (qw, qz, s))
+        for M in (1, 12, 300):
+            x = O.make_x(M, K, seed=M + dev_index)
+            with torch.cuda.device(d):
+                out = awq_b200.gemm(torch.from_numpy(x).to(d), dqw, dqz, ds, 128)
+            assert out.device == d
+            assert O.max_rel_err(out.float().cpu().numpy(), O.awq_gemm_f32(x, qw, qz, s)) <= TOL
