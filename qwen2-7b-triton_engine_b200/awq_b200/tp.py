@@ -129,13 +129,21 @@ class ColumnParallelAWQ:
         self.gemm_bias = _default_gemm_bias() if gemm is None else None
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
-        if self.w.bias is not None and self.gemm_bias is not None:
-            return self.gemm_bias(x, self.w.qweight, self.w.qzeros, self.w.scales, self.w.bias,
-                                  self.w.group_size)
-        out = self.gemm(x, self.w.qweight, self.w.qzeros, self.w.scales, self.w.group_size)
-        if self.w.bias is not None:                   # bias added after the GEMM (model/qwen2.py:45-46)
-            out = out + self.w.bias
-        return out
+        return _column_forward(self.w, self.gemm, self.gemm_bias, x)
+
+
+def _column_forward(w: AWQWeights, gemm, gemm_bias, x: torch.Tensor) -> torch.Tensor:
+    """x @ W (+ bias) for a column shard: the bias in the product's epilogue with the
+    library, after the product with a substituted one (model/qwen2.py:45-46)."""
+    N = w.scales.shape[1]
+    if N == 0:                                        # more ranks than heads / columns
+        return torch.zeros((*x.shape[:-1], 0), dtype=torch.float16, device=x.device)
+    if w.bias is not None and gemm_bias is not None:
+        return gemm_bias(x, w.qweight, w.qzeros, w.scales, w.bias, w.group_size)
+    out = gemm(x, w.qweight, w.qzeros, w.scales, w.group_size)
+    if w.bias is not None:
+        out = out + w.bias
+    return out
 
 
 class RowParallelAWQ:
@@ -148,9 +156,15 @@ class RowParallelAWQ:
     only, so every rank takes the same one."""
 
     def __init__(self, full: AWQWeights, world: int, rank: int, group: Optional[object] = None,
-                 gemm: Optional[GemmFn] = None, comm=None):
+                 gemm: Optional[GemmFn] = None, comm=None,
+                 k_bounds: Optional[tuple[int, int]] = None):
         K = full.qweight.shape[0]
-        self.k0, self.k1 = row_bounds(K, full.group_size, world, rank)
+        # default: whole quantization groups dealt evenly; k_bounds: the caller's split
+        # (whole attention heads for o, see AttentionLinearsTP), group-aligned
+        self.k0, self.k1 = k_bounds if k_bounds is not None else row_bounds(K, full.group_size,
+                                                                            world, rank)
+        if self.k0 % full.group_size or self.k1 % full.group_size or not 0 <= self.k0 <= self.k1 <= K:
+            raise ValueError(f"row bounds [{self.k0}, {self.k1}) are not whole groups of {K}")
         qw, qz, s = shard_rows(full.qweight, full.qzeros, full.scales, self.k0, self.k1,
                                full.group_size)
         self.w = AWQWeights(qw, qz, s, full.group_size, full.bias if rank == 0 else None)
@@ -191,6 +205,99 @@ class RowParallelAWQ:
         if self.world > 1:
             dist.all_reduce(out, op=dist.ReduceOp.SUM, group=self.group)
         return out
+
+
+def head_bounds(num_heads: int, world: int, rank: int) -> tuple[int, int]:
+    """[h0, h1) attention heads of `rank`: whole heads dealt as evenly as possible
+    (Qwen2-7B's 28 query heads at 8 ranks: 4,4,4,4,3,3,3,3)."""
+    return even_split(num_heads, world, rank)
+
+
+def kv_head_bounds(num_heads: int, num_kv_heads: int, h0: int, h1: int) -> tuple[int, int]:
+    """[g0, g1) key/value heads that query heads [h0, h1) read under grouped-query
+    attention: query head h uses key/value head h // (num_heads / num_kv_heads)
+    (model/qwen2.py:131-138 expands each kv head to its group of query heads)."""
+    if num_heads % num_kv_heads:
+        raise ValueError(f"{num_heads} query heads do not group over {num_kv_heads} kv heads")
+    if h1 <= h0:
+        return 0, 0
+    g = num_heads // num_kv_heads
+    return h0 // g, (h1 - 1) // g + 1
+
+
+@dataclass
+class QKVShard:
+    """A rank's slice of the fused q/k/v projection in whole heads: its query heads
+    [q_heads) and the key/value heads [kv_heads) they use.  The local fused matrix keeps
+    the reference's order -- q columns, then k, then v (model/qwen2.py:81-83) -- so the
+    local product splits at q_size and q_size + kv_size as the reference's does
+    (:111-113)."""
+    q_heads: tuple[int, int]
+    kv_heads: tuple[int, int]
+    head_dim: int
+    weights: AWQWeights
+
+    @property
+    def q_size(self) -> int:
+        return (self.q_heads[1] - self.q_heads[0]) * self.head_dim
+
+    @property
+    def kv_size(self) -> int:
+        return (self.kv_heads[1] - self.kv_heads[0]) * self.head_dim
+
+
+def shard_qkv_by_heads(full: AWQWeights, num_heads: int, num_kv_heads: int, head_dim: int,
+                       world: int, rank: int) -> QKVShard:
+    """Column shard of the fused q/k/v weights (and bias) by whole heads.  Key/value heads
+    shared by the query heads of two ranks are held by both (replicated), so every rank
+    can attend over its own query heads without communication."""
+    if head_dim % 8:
+        raise ValueError(f"head_dim={head_dim} is not a whole number of packed words")
+    q_size, kv_size = num_heads * head_dim, num_kv_heads * head_dim
+    if full.scales.shape[1] != q_size + 2 * kv_size:
+        raise ValueError(f"fused q/k/v has {full.scales.shape[1]} columns, expected "
+                         f"{q_size + 2 * kv_size}")
+    h0, h1 = head_bounds(num_heads, world, rank)
+    g0, g1 = kv_head_bounds(num_heads, num_kv_heads, h0, h1)
+    cols = [(h0 * head_dim, h1 * head_dim),
+            (q_size + g0 * head_dim, q_size + g1 * head_dim),
+            (q_size + kv_size + g0 * head_dim, q_size + kv_size + g1 * head_dim)]
+    parts = [shard_columns(full.qweight, full.qzeros, full.scales, a, b) for a, b in cols]
+    qw, qz, sc = (torch.cat([p[i] for p in parts], 1) for i in range(3))
+    bias = None
+    if full.bias is not None:
+        bias = torch.cat([full.bias[a:b] for a, b in cols])
+    return QKVShard((h0, h1), (g0, g1), head_dim, AWQWeights(qw, qz, sc, full.group_size, bias))
+
+
+class AttentionLinearsTP:
+    """The attention block's two AWQ projections over `world` ranks, split by whole heads
+    (the reference runs them on one GPU, model/qwen2.py:81-113,156): the fused q/k/v
+    projection column-parallel over the rank's query heads plus the key/value heads they
+    use, and o row-parallel over the same query heads' rows, followed by the all-reduce.
+    Attention itself (RoPE, cache, softmax) runs on the rank's heads in between."""
+
+    def __init__(self, qkv: AWQWeights, o: AWQWeights, num_heads: int, num_kv_heads: int,
+                 head_dim: int, world: int, rank: int, group: Optional[object] = None,
+                 gemm: Optional[GemmFn] = None, comm=None):
+        if o.qweight.shape[0] != num_heads * head_dim:
+            raise ValueError("o must have K == num_heads * head_dim")
+        self.shard = shard_qkv_by_heads(qkv, num_heads, num_kv_heads, head_dim, world, rank)
+        h0, h1 = self.shard.q_heads
+        self.gemm = gemm or _default_gemm()
+        self.gemm_bias = _default_gemm_bias() if gemm is None else None
+        self.o = RowParallelAWQ(o, world, rank, group=group, gemm=gemm, comm=comm,
+                                k_bounds=(h0 * head_dim, h1 * head_dim))
+
+    def project_qkv(self, x: torch.Tensor):
+        """(q, k, v) of this rank's heads: [..., q_size], [..., kv_size], [..., kv_size]."""
+        out = _column_forward(self.shard.weights, self.gemm, self.gemm_bias, x)
+        qs, ks = self.shard.q_size, self.shard.kv_size
+        return out[..., :qs], out[..., qs:qs + ks], out[..., qs + ks:]
+
+    def project_o(self, attn_local: torch.Tensor) -> torch.Tensor:
+        """o of the rank's heads' attention output [..., q_size], summed over the ranks."""
+        return self.o(attn_local)
 
 
 class TensorParallelMLP:

@@ -162,3 +162,90 @@ def test_dead_rank_surfaces_as_error_not_hang():
     assert msgs[1] == "raised"
     assert msgs[0].startswith("error"), msgs[0]
     assert time.time() - t0 < 90
+
+
+# ---- attention projections split by whole heads (Qwen2-7B: 28 query heads, 4 kv heads) ----
+NQ, NKV, HD = 28, 4, 128
+
+
+def test_head_shards_partition_and_follow_gqa():
+    from awq_b200 import tp
+    for world in (1, 2, 3, 4, 7, 8):
+        bounds = [tp.head_bounds(NQ, world, r) for r in range(world)]
+        assert bounds[0][0] == 0 and bounds[-1][1] == NQ
+        assert all(bounds[i][1] == bounds[i + 1][0] for i in range(world - 1))
+        for h0, h1 in bounds:
+            g0, g1 = tp.kv_head_bounds(NQ, NKV, h0, h1)
+            assert {h // (NQ // NKV) for h in range(h0, h1)} == set(range(g0, g1))
+    assert [tp.head_bounds(NQ, 8, r)[1] - tp.head_bounds(NQ, 8, r)[0] for r in range(8)] == \
+        [4, 4, 4, 4, 3, 3, 3, 3]
+
+
+def test_qkv_head_shards_are_the_right_columns():
+    import numpy as np
+    from awq_b200 import tp
+    K, N = 256, (NQ + 2 * NKV) * HD
+    qw, qz, s = _layer(K, N, seed=41)
+    bias = torch.from_numpy(np.random.default_rng(2).uniform(-1, 1, N).astype(np.float16))
+    full = O.awq_dequant(qw.numpy(), qz.numpy(), s.numpy())
+    qsz, kvsz = NQ * HD, NKV * HD
+    for world in (2, 3, 8):
+        for r in range(world):
+            sh = tp.shard_qkv_by_heads(tp.AWQWeights(qw, qz, s, 128, bias), NQ, NKV, HD, world, r)
+            (h0, h1), (g0, g1) = sh.q_heads, sh.kv_heads
+            cols = np.r_[h0 * HD:h1 * HD, qsz + g0 * HD:qsz + g1 * HD,
+                         qsz + kvsz + g0 * HD:qsz + kvsz + g1 * HD]
+            got = O.awq_dequant(sh.weights.qweight.numpy(), sh.weights.qzeros.numpy(),
+                                sh.weights.scales.numpy())
+            assert np.array_equal(got.view(np.uint16), full[:, cols].view(np.uint16))
+            assert torch.equal(sh.weights.bias, bias[torch.from_numpy(cols)])
+            assert sh.q_size == (h1 - h0) * HD and sh.kv_size == (g1 - g0) * HD
+
+
+def _attn_worker(rank, world, port, seed, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=30))
+    try:
+        from awq_b200 import tp
+        qkv = _layer(256, (NQ + 2 * NKV) * HD, seed)
+        o = _layer(NQ * HD, 256, seed + 1)
+        x = torch.from_numpy(O.make_x(2, 256, seed=seed + 2))
+        attn = torch.from_numpy(O.make_x(2, NQ * HD, seed=seed + 3))   # stands in for attention
+        lin = tp.AttentionLinearsTP(tp.AWQWeights(*qkv), tp.AWQWeights(*o), NQ, NKV, HD, world,
+                                    rank, gemm=_cpu_gemm)
+        qv, kv, vv = lin.project_qkv(x)
+        h0, h1 = lin.shard.q_heads
+        y = lin.project_o(attn[:, h0 * HD:h1 * HD].contiguous())
+        q.put((rank, lin.shard.q_heads, lin.shard.kv_heads, qv.float().numpy(),
+               kv.float().numpy(), vv.float().numpy(), y.float().numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_attention_linears_by_heads_gloo_world4():
+    world, seed = 4, 51
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_attn_worker, args=(r, world, port, seed, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    qkv = _layer(256, (NQ + 2 * NKV) * HD, seed)
+    o = _layer(NQ * HD, 256, seed + 1)
+    x = torch.from_numpy(O.make_x(2, 256, seed=seed + 2))
+    attn = torch.from_numpy(O.make_x(2, NQ * HD, seed=seed + 3))
+    full = _cpu_gemm(x, *qkv, 128).float().numpy()
+    y_ref = _cpu_gemm(attn, *o, 128).float().numpy()
+    qsz, kvsz = NQ * HD, NKV * HD
+    for rank, (h0, h1), (g0, g1), qv, kv, vv, y in got:
+        assert O.max_rel_err(qv, full[:, h0 * HD:h1 * HD]) <= 1e-2
+        assert O.max_rel_err(kv, full[:, qsz + g0 * HD:qsz + g1 * HD]) <= 1e-2
+        assert O.max_rel_err(vv, full[:, qsz + kvsz + g0 * HD:qsz + kvsz + g1 * HD]) <= 1e-2
+        assert O.max_rel_err(y, y_ref) <= 1e-2
