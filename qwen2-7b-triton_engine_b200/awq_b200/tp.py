@@ -13,6 +13,11 @@ AWQ drop-in, in the packed layout the reference registers (model/qwen2.py:34-36)
   possible (Qwen2-7B down has 148 groups: 19/18 at 8 ranks).  Each rank's product is
   a partial sum and one all-reduce (sum) of the fp16 [M, N] output finishes it.
 
+* attention by whole heads (``AttentionLinearsTP``): the fused q/k/v columns of the
+  rank's query heads and of the key/value heads they read under grouped-query attention
+  (model/qwen2.py:131-138), and o's rows of the same query heads, so attention itself
+  runs per rank with no exchange until o's all-reduce.
+
 The product runs through ``kernels.awq_gemm.awq_gemm_forward`` (the sm_100a
 library); ``gemm=`` lets host-logic tests substitute a CPU function under ``gloo``.
 """
