@@ -202,6 +202,12 @@ def test_qkv_head_shards_are_the_right_columns():
             assert sh.q_size == (h1 - h0) * HD and sh.kv_size == (g1 - g0) * HD
 
 
+def _qkv_bias():
+    import numpy as np
+    return torch.from_numpy(np.random.default_rng(9).uniform(-1, 1, (NQ + 2 * NKV) * HD)
+                            .astype(np.float16))
+
+
 def _attn_worker(rank, world, port, seed, q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -214,8 +220,8 @@ def _attn_worker(rank, world, port, seed, q):
         o = _layer(NQ * HD, 256, seed + 1)
         x = torch.from_numpy(O.make_x(2, 256, seed=seed + 2))
         attn = torch.from_numpy(O.make_x(2, NQ * HD, seed=seed + 3))   # stands in for attention
-        lin = tp.AttentionLinearsTP(tp.AWQWeights(*qkv), tp.AWQWeights(*o), NQ, NKV, HD, world,
-                                    rank, gemm=_cpu_gemm)
+        lin = tp.AttentionLinearsTP(tp.AWQWeights(*qkv, 128, _qkv_bias()), tp.AWQWeights(*o), NQ,
+                                    NKV, HD, world, rank, gemm=_cpu_gemm)
         qv, kv, vv = lin.project_qkv(x)
         h0, h1 = lin.shard.q_heads
         y = lin.project_o(attn[:, h0 * HD:h1 * HD].contiguous())
@@ -241,7 +247,7 @@ def test_attention_linears_by_heads_gloo_world4():
     o = _layer(NQ * HD, 256, seed + 1)
     x = torch.from_numpy(O.make_x(2, 256, seed=seed + 2))
     attn = torch.from_numpy(O.make_x(2, NQ * HD, seed=seed + 3))
-    full = _cpu_gemm(x, *qkv, 128).float().numpy()
+    full = (_cpu_gemm(x, *qkv, 128) + _qkv_bias()).float().numpy()     # q/k/v carry a bias
     y_ref = _cpu_gemm(attn, *o, 128).float().numpy()
     qsz, kvsz = NQ * HD, NKV * HD
     for rank, (h0, h1), (g0, g1), qv, kv, vv, y in got:
