@@ -147,3 +147,41 @@ int main(void) {
                     f"-Wl,-rpath,{lib.parent}"], check=True)
     out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split()
     assert int(out[0]) >= 100 and out[1:] == ["1", "1", "msg"]
+
+
+@pytest.mark.parametrize("K,N,gs,why", [
+    (0, 64, 128, b"positive"),            # empty K
+    (256, 0, 128, b"positive"),           # empty N
+    (256, 60, 128, b"multiple of 8"),     # N not whole packed words
+    (256, 64, 0, b"group_size"),          # no groups
+    (256, 64, 12, b"group_size"),         # group not a multiple of 8
+    (200, 64, 128, b"multiple of group_size"),
+    ((1 << 30) + 128, 64, 128, b"2^30"),  # sizes above the library's index range
+])
+def test_weight_shape_checks_without_a_device(K, N, gs, why):
+    import awq_b200._lib as L
+    lib = L.load()
+    for rc in (lib.awq_gemm_f16(16, K, 16, 16, 16, 16, N, 1, N, K, gs, None, 0, None),
+               lib.awq_dequant_f16(16, 16, 16, 16, K, N, gs, None)):
+        assert rc == L.AWQ_ERR_INVALID_ARG
+        assert why in lib.awq_last_error()
+
+
+def test_activation_and_output_checks_without_a_device():
+    import awq_b200._lib as L
+    lib = L.load()
+    ok = (16, 16, 16)                                            # aligned weight pointers
+    cases = [
+        ((16, 256, *ok, 16, 64, 0, 64, 256, 128), b"M="),        # M = 0
+        ((16, 255, *ok, 16, 64, 1, 64, 256, 128), b"ldx"),       # ldx < K
+        ((16, 256, *ok, 16, 63, 1, 64, 256, 128), b"ldx"),       # ldo < N
+        ((17, 256, *ok, 16, 64, 1, 64, 256, 128), b"aligned"),   # odd x address
+        ((16, 256, *ok, None, 64, 1, 64, 256, 128), b"null"),    # no output
+    ]
+    for args, why in cases:
+        assert lib.awq_gemm_f16(*args, None, 0, None) == L.AWQ_ERR_INVALID_ARG, why
+        assert why in lib.awq_last_error(), (why, lib.awq_last_error())
+    # a bias pointer is required by the biased entry point
+    assert lib.awq_gemm_f16_bias(16, 256, *ok, None, 16, 64, 1, 64, 256, 128, None, 0, None) == \
+        L.AWQ_ERR_INVALID_ARG
+    assert b"bias" in lib.awq_last_error()
