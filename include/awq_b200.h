@@ -4,10 +4,14 @@
  * Drop-in boundary for songqiuyu/Qwen2-7B-Triton_Engine's AWQ matrix product.
  * Every entry point takes plain pointers and sizes; device pointers are owned by
  * the caller and never freed here.  Streams are passed as `void*` holding a
- * cudaStream_t (NULL = the legacy default stream).  No entry point allocates
- * device memory, synchronizes the device, or throws; each returns AWQ_OK (0) or
- * a negative AWQ_ERR_* code, and awq_last_error() gives a message for the
- * calling thread.
+ * cudaStream_t (NULL = the legacy default stream).  The product entry points
+ * allocate no device memory and never synchronize: they only enqueue kernels on
+ * `stream`.  The exceptions are named where they are declared: the
+ * tensor-parallel set-up and tear-down (awq_tp_comm_create / _open / _destroy)
+ * allocate, map or free a buffer and synchronize the device, and
+ * awq_device_status synchronizes `stream`.  Nothing throws; each entry point
+ * returns AWQ_OK (0) or a negative AWQ_ERR_* code, and awq_last_error() gives a
+ * message for the calling thread.
  *
  * Packed layout (model/qwen2.py:34-36, kernels/awq_gemm.py:36-38):
  *   qweight int32 [K, N/8]   row-major; element n of row k is the nibble at bit
@@ -132,17 +136,19 @@ AWQ_API int awq_gemm_f16_silu_mul(const void* x, int64_t ldx, const int32_t* qwe
 
 /*
  * awq_gemm_f16 for callers that cannot allocate device memory: same inputs and
- * output, no workspace argument.  No counterpart in the reference (its M<=4 path
- * allocates a global K*N buffer, kernels/awq_gemm.py:255-262).  Meant for hosts that
- * forbid allocation on the path where the product runs -- an engine that plans all
- * device memory up front (cudaMalloc / cudaFree can synchronize the device), or a
- * plugin interface that hands the library only its input and output buffers.
+ * output, no workspace argument.  This entry point has no counterpart in the
+ * reference.  It serves hosts that forbid allocation on the path where the product
+ * runs -- an engine that plans all device memory up front (cudaMalloc / cudaFree can
+ * synchronize the device and stall every stream), or a plugin interface that hands
+ * the library only its input and output buffers.
  *   - Runs the generic decode kernel (any M, 16-row chunks; fastest for M <= 16).
  *   - Its split-K scratch is a 4 MiB file-scope device array, held by every GPU that
  *     loads the library until the process exits.  The split factor is reduced until the
  *     partial sums fit; a shape that still does not fit returns AWQ_ERR_WORKSPACE.
- *   - The first call on a device looks up the array's address and zero-fills its
- *     counters (synchronous cudaMemset): make it before any stream capture.
+ *   - The first call on a device looks up the array's device address (with that
+ *     device current): make that first call before any stream capture.  The array's
+ *     counters start at zero because a device array is zero-initialised when the
+ *     library's module loads, and every call leaves them at zero again.
  *   - All calls share the array: calls that overlap on the GPU race and give wrong
  *     results.  No allocation of any kind happens inside.
  */
@@ -168,10 +174,14 @@ AWQ_API int awq_device_status(void* stream, int* status_out);
  * For the row-parallel linears of a tensor-parallel model (o_proj and down_proj split
  * along K over `world` GPUs of one box, one process per GPU), awq_gemm_f16_allreduce
  * computes this rank's partial product and sums it over all ranks in the same kernel:
- * the last CTA of each output tile stores its fp32 tile into every rank's receive buffer
- * over NVLink (CUDA IPC peer mappings, plain stores), adds 1 to every rank's counter for
- * the tile, waits (bounded) until all ranks' tiles are in its own buffer and sums them in
- * rank order, so every rank writes the same fp16 bits.  It replaces the awq_gemm_f16 +
+ * the CTA that finishes an output tile stores each fp32 value of the tile, packed with
+ * the call's flag (the call number + 1) into one 8-byte word, into its slot of every
+ * rank's receive buffer over NVLink (CUDA IPC peer mappings, plain stores); it then
+ * reads, in its own buffer, every rank's words for the tile until their flags show this
+ * call (bounded wait) and sums the values in rank order, so every rank writes the same
+ * fp16 bits.  A wait that runs out sets status bit 4 (awq_device_status): the output of
+ * that call is then wrong on this rank and the communicator must be reset
+ * (awq_tp_comm_reset) on every rank before it is used again.  It replaces the awq_gemm_f16 +
  * NCCL all-reduce pair of a row-parallel layer (the reference has no tensor
  * parallelism: inference/engine.py:15).
  *
@@ -193,6 +203,15 @@ AWQ_API int awq_tp_comm_create(int world, int rank, int64_t max_n, void* handle_
 AWQ_API int awq_tp_comm_open(awq_tp_comm* comm, const void* handles);
 /* Longest wait for the other ranks' tiles, in ns (default 2 s); then status bit 4. */
 AWQ_API int awq_tp_comm_set_timeout(awq_tp_comm* comm, uint64_t timeout_ns);
+/*
+ * Return this rank's communicator to its freshly opened state after a wait ran out
+ * (status bit 4): synchronizes the device, zeroes this rank's receive buffer and call
+ * number, synchronizes again.  A collective step: every rank must call it with no fused
+ * call in flight anywhere, between two barriers of the ranks (one before, so that no
+ * rank still writes into another's buffer, one after, so that no rank starts a new call
+ * before every buffer is clear).  No counterpart in the reference.
+ */
+AWQ_API int awq_tp_comm_reset(awq_tp_comm* comm);
 AWQ_API int awq_tp_comm_destroy(awq_tp_comm* comm);
 
 /* 1 if awq_gemm_f16_allreduce can run this call (the decode kernel with one CTA per SM

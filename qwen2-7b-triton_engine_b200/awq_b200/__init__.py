@@ -330,6 +330,58 @@ class TPComm:
                 self._ptr, x2d.data_ptr(), x2d.stride(0), qweight.data_ptr(), x2d.shape[0], N,
                 qweight.shape[0], int(group_size)))
 
+    def supported_shape(self, M: int, N: int, K: int, group_size: int = 128) -> bool:
+        """``supported`` for a dense, 16-byte aligned x [M, K] and qweight [K, N/8]: the
+        shape part of the decision alone.  ``awq_allreduce_supported`` only inspects the
+        pointers' alignment, so aligned placeholders stand in for them; a caller that
+        evaluates this for every rank's K gets the same answer on every rank."""
+        if not self.opened or K <= 0 or M <= 0:
+            return False
+        with _DeviceGuard(self.device):
+            return bool(_lib.load().awq_allreduce_supported(
+                self._ptr, 256, K, 256, int(M), int(N), int(K), int(group_size)))
+
+    def check(self, group=None, collective: bool = False) -> None:
+        """Synchronise the current stream and raise ``AwqError`` if a kernel on this
+        device reported an error since the last check: status bit 4 (a fused all-reduce
+        gave up waiting for another rank -- that call's output is wrong and every rank
+        must ``reset`` the communicator) or bit 1 (a bounded wait inside a kernel ran
+        out).  The status word is cleared.  Call it where the caller synchronises anyway
+        (after a decode step, before its result is read).
+
+        Only the rank whose wait ran out sees bit 4; a rank that ran ahead may have summed
+        a stale tile without waiting.  With ``collective=True`` (every rank calls it, same
+        ``group``) the ranks' status bits are combined with one all-reduce, so every rank
+        raises together and can take part in ``reset``."""
+        st = device_status(self.device)
+        if collective:
+            import torch.distributed as dist
+            bits = torch.tensor([(st >> b) & 1 for b in range(3)], dtype=torch.int32,
+                                device=self.device)
+            dist.all_reduce(bits, op=dist.ReduceOp.MAX, group=group)
+            st = sum(int(v) << b for b, v in enumerate(bits.tolist()))
+        if st:
+            what = []
+            if st & _lib.STATUS_PEER_TIMEOUT:
+                what.append("a fused all-reduce timed out waiting for another rank "
+                            "(reset the communicator on every rank)")
+            if st & _lib.STATUS_BARRIER_TIMEOUT:
+                what.append("a bounded wait inside a kernel ran out")
+            if st & _lib.STATUS_SHAPE:
+                what.append("a kernel rejected its parameters")
+            raise AwqError(_lib.AWQ_ERR_DEVICE, f"device status {st}: " + "; ".join(what))
+
+    def reset(self, group=None) -> None:
+        """Collective: return every rank's communicator to its freshly opened state (after
+        ``check`` raised for a peer time-out).  Every rank must call it; no fused call may
+        be in flight.  Barrier, clear this rank's receive buffer and call number, barrier."""
+        import torch.distributed as dist
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=group)
+        with _DeviceGuard(self.device):
+            _lib.check(_lib.load().awq_tp_comm_reset(self._ptr))
+        dist.barrier(group=group)
+
     def close(self) -> None:
         if self._ptr is not None:
             with _DeviceGuard(self.device):

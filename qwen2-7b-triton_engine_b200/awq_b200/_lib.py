@@ -47,6 +47,7 @@ SIGNATURES = {
     "awq_tp_comm_create": ([_INT, _INT, _I64, _P, ctypes.POINTER(_P)], _INT),
     "awq_tp_comm_open": ([_P, _P], _INT),
     "awq_tp_comm_set_timeout": ([_P, ctypes.c_uint64], _INT),
+    "awq_tp_comm_reset": ([_P], _INT),
     "awq_tp_comm_destroy": ([_P], _INT),
     "awq_allreduce_supported": ([_P, _P, _I64, _P, _I64, _I64, _I64, _I64], _INT),
     "awq_gemm_f16_allreduce": ([_P, _P, _I64, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P,

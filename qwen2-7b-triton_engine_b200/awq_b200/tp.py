@@ -154,15 +154,20 @@ def _column_forward(w: AWQWeights, gemm, gemm_bias, x: torch.Tensor) -> torch.Te
 class RowParallelAWQ:
     """Rank's K-row slice of an AWQ linear; the partial outputs are all-reduced.
 
-    With ``comm`` (an ``awq_b200.TPComm``) a call the fused kernel supports -- decode,
-    M <= 16 per launch -- runs the product and the all-reduce in one kernel
-    (``awq_b200.gemm_allreduce``: peer stores over NVLink, sum in rank order); other
-    calls use the library product and an NCCL all-reduce.  The choice depends on shapes
-    only, so every rank takes the same one."""
+    With ``comm`` (an ``awq_b200.TPComm``) a call the fused kernel supports runs the
+    product and the all-reduce in one kernel (``awq_b200.gemm_allreduce``: peer stores
+    over NVLink, sum in rank order); other calls use the library product and an NCCL
+    all-reduce.  The choice must be the same on every rank -- a rank in the fused kernel
+    waits for the others' tiles while a rank in NCCL waits for the others' NCCL call --
+    so it is made from quantities every rank knows alike: M, N, the group size and every
+    rank's K (gathered once at construction).  A rank without rows makes every rank use
+    NCCL.  ``check=True`` reads the device status after each fused call (a
+    synchronisation) and raises on a time-out; otherwise call ``comm.check()`` where the
+    caller synchronises anyway."""
 
     def __init__(self, full: AWQWeights, world: int, rank: int, group: Optional[object] = None,
                  gemm: Optional[GemmFn] = None, comm=None,
-                 k_bounds: Optional[tuple[int, int]] = None):
+                 k_bounds: Optional[tuple[int, int]] = None, check: bool = False):
         K = full.qweight.shape[0]
         # default: whole quantization groups dealt evenly; k_bounds: the caller's split
         # (whole attention heads for o, see AttentionLinearsTP), group-aligned
@@ -178,19 +183,44 @@ class RowParallelAWQ:
         self.world = world
         self.gemm = gemm or _default_gemm()
         self.comm = comm
+        self.check = check
+        self.k_all: Optional[list[int]] = None     # every rank's K, rank order
+        if comm is not None and world > 1:
+            ks = [None] * world
+            dist.all_gather_object(ks, self.k1 - self.k0, group=group)
+            self.k_all = [int(k) for k in ks]
+        self._fused_ok: dict = {}
+
+    def fused_for(self, M: int) -> bool:
+        """Whether a call with M activation rows runs the fused kernel (the same answer on
+        every rank: it depends on M, N, the group size and every rank's K only)."""
+        if self.comm is None or self.world < 2 or self.k_all is None:
+            return False
+        ok = self._fused_ok.get(M)
+        if ok is None:
+            N = self.w.scales.shape[1]
+            ok = all(k > 0 and self.comm.supported_shape(M, N, k, self.w.group_size)
+                     for k in self.k_all)
+            self._fused_ok[M] = ok
+        return ok
 
     def _fused(self, x_local: torch.Tensor) -> Optional[torch.Tensor]:
         import awq_b200
-        if self.comm is None or self.world < 2 or self.k1 <= self.k0:
+        M = 1
+        for d in x_local.shape[:-1]:
+            M *= int(d)
+        if not self.fused_for(M):
             return None
-        x2 = x_local.reshape(-1, x_local.shape[-1])
-        if x2.stride(1) != 1 or x2.data_ptr() % 16 or (x2.stride(0) * 2) % 16:
+        x2 = x_local.reshape(M, x_local.shape[-1])
+        # the decision assumed a dense, 16-byte aligned x: make it so
+        if x2.stride(1) != 1 or x2.data_ptr() % 16 or (x2.stride(0) * 2) % 16 \
+                or x2.stride(0) != x2.shape[1]:
             x2 = x2.contiguous().clone()
         N = self.w.scales.shape[1]
-        if not self.comm.supported(x2, self.w.qweight, N, self.w.group_size):
-            return None
         out = awq_b200.gemm_allreduce(x2, self.w.qweight, self.w.qzeros, self.w.scales,
                                       self.w.group_size, self.comm)
+        if self.check:
+            self.comm.check()
         out = out.view(*x_local.shape[:-1], N)
         return out + self.bias if self.bias is not None else out
 
@@ -284,7 +314,7 @@ class AttentionLinearsTP:
 
     def __init__(self, qkv: AWQWeights, o: AWQWeights, num_heads: int, num_kv_heads: int,
                  head_dim: int, world: int, rank: int, group: Optional[object] = None,
-                 gemm: Optional[GemmFn] = None, comm=None):
+                 gemm: Optional[GemmFn] = None, comm=None, check: bool = False):
         if o.qweight.shape[0] != num_heads * head_dim:
             raise ValueError("o must have K == num_heads * head_dim")
         self.shard = shard_qkv_by_heads(qkv, num_heads, num_kv_heads, head_dim, world, rank)
@@ -292,7 +322,7 @@ class AttentionLinearsTP:
         self.gemm = gemm or _default_gemm()
         self.gemm_bias = _default_gemm_bias() if gemm is None else None
         self.o = RowParallelAWQ(o, world, rank, group=group, gemm=gemm, comm=comm,
-                                k_bounds=(h0 * head_dim, h1 * head_dim))
+                                k_bounds=(h0 * head_dim, h1 * head_dim), check=check)
 
     def project_qkv(self, x: torch.Tensor):
         """(q, k, v) of this rank's heads: [..., q_size], [..., kv_size], [..., kv_size]."""
@@ -314,7 +344,7 @@ class TensorParallelMLP:
 
     def __init__(self, gate_up: AWQWeights, down: AWQWeights, intermediate: int, world: int,
                  rank: int, group: Optional[object] = None, gemm: Optional[GemmFn] = None,
-                 comm=None):
+                 comm=None, check: bool = False):
         if down.qweight.shape[0] != intermediate:
             raise ValueError("down must have K == intermediate")
         gs = down.group_size
@@ -325,7 +355,8 @@ class TensorParallelMLP:
         self.gate_up = ColumnParallelAWQ(gate_up, world, rank, parts=[intermediate, intermediate],
                                          gemm=gemm, bounds=bounds)
         self.inter_local = self.gate_up.parts_local[0]
-        self.down = RowParallelAWQ(down, world, rank, group=group, gemm=gemm, comm=comm)
+        self.down = RowParallelAWQ(down, world, rank, group=group, gemm=gemm, comm=comm,
+                                   check=check)
         assert (self.down.k1 - self.down.k0) == self.inter_local
         # the library computes silu(gate) * up with the product; a substituted product
         # (host-logic tests) goes through the slices below

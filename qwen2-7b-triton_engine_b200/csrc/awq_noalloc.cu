@@ -14,12 +14,15 @@
 //     until the partial sums fit, and a shape that does not fit even then is rejected
 //     with AWQ_ERR_WORKSPACE and a message naming the size it would need;
 //   * the first call on a device looks up the array's device address
-//     (cudaGetSymbolAddress, with that device current) and zero-fills the counter
-//     region with a synchronous cudaMemset -- make that first call before any stream
-//     capture;
-//   * every call shares the one array and leaves its counters at zero; calls that
-//     overlap on the GPU (different streams, or graph branches without an order between
-//     them) race on it and give wrong results.
+//     (cudaGetSymbolAddress, with that device current) -- make that first call before
+//     any stream capture;
+//   * the split-K counters at the head of the array start at zero because a __device__
+//     array is zero-initialised when the module loads, and the generic kernel (which has
+//     no wait that can give up) leaves every counter it used at zero; nothing here writes
+//     the array from the host;
+//   * every call shares the one array; calls that overlap on the GPU (different streams,
+//     or graph branches without an order between them) race on it and give wrong
+//     results.
 // The kernel is the generic decode kernel of awq_gemv.cu (mma.sync, split-K); any M is
 // accepted (16-row chunks), so large M is correct but slow here.
 #include <cuda_runtime.h>
@@ -33,7 +36,6 @@
 namespace {
 
 constexpr size_t kNoAllocScratchBytes = 4u << 20;              // 4 MiB per device
-constexpr size_t kNoAllocCounterBytes = 16384 * sizeof(int);   // head of the workspace
 
 __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
@@ -63,9 +65,6 @@ int slot_for_current_device(ScratchSlot** out) {
     if (e != cudaSuccess) return fail(AWQ_ERR_CUDA, cudaGetErrorString(e));
     int sms = 0;
     e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (e != cudaSuccess) return fail(AWQ_ERR_CUDA, cudaGetErrorString(e));
-    // split-K arrival counters must start at zero (each completed call leaves them so)
-    e = cudaMemset(p, 0, kNoAllocCounterBytes);
     if (e != cudaSuccess) return fail(AWQ_ERR_CUDA, cudaGetErrorString(e));
     s.ptr = p;
     s.num_sms = sms;

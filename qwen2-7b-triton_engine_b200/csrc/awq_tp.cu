@@ -111,6 +111,21 @@ int awq_tp_comm_set_timeout(awq_tp_comm* c, uint64_t timeout_ns) {
   return AWQ_OK;
 }
 
+int awq_tp_comm_reset(awq_tp_comm* c) {
+  if (!c || !c->ready) return fail_tp(AWQ_ERR_INVALID_ARG, "communicator missing or not opened");
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail_tp_cuda(e, "cudaGetDevice");
+  if (dev != c->device) return fail_tp(AWQ_ERR_INVALID_ARG, "current device is not the communicator's");
+  // every kernel of this device (this rank's fused calls included) must be finished
+  // before the buffer is cleared; the caller keeps the other ranks out with a barrier
+  e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemset(c->local, 0, c->bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return fail_tp_cuda(e, "communicator reset");
+  return AWQ_OK;
+}
+
 int awq_tp_comm_destroy(awq_tp_comm* c) {
   if (!c) return AWQ_OK;
   cudaError_t first = cudaSuccess;

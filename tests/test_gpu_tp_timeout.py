@@ -37,8 +37,18 @@ def test_fused_allreduce_wait_times_out_with_status(cuda):
         awq_b200.gemm_allreduce(x, qw, qz, s, 128, c0)
         torch.cuda.synchronize()
         waited = time.perf_counter() - t0
-        assert awq_b200.device_status() & L.STATUS_PEER_TIMEOUT
         assert waited < 10.0
+        # the time-out surfaces as an exception from the communicator's check ...
+        with pytest.raises(awq_b200.AwqError, match="timed out waiting for another rank"):
+            c0.check()
+        assert awq_b200.device_status() == 0          # check() read and cleared the word
+        # ... and both ranks' communicators go back to their opened state (the collective
+        # TPComm.reset puts a barrier of the ranks around this call; here one process
+        # holds both ranks)
+        lib = L.load()
+        for c in (c0, c1):
+            L.check(lib.awq_tp_comm_reset(c._ptr))
+        assert awq_b200.device_status() == 0
         # the device and the library are fine afterwards
         ref = O.awq_gemm_f32(x.cpu().numpy(), *(a.cpu().numpy() for a in (qw, qz, s)))
         out = awq_b200.gemm(x, qw, qz, s, 128)

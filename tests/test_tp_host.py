@@ -255,3 +255,52 @@ def test_attention_linears_by_heads_gloo_world4():
         assert O.max_rel_err(kv, full[:, qsz + g0 * HD:qsz + g1 * HD]) <= 1e-2
         assert O.max_rel_err(vv, full[:, qsz + kvsz + g0 * HD:qsz + kvsz + g1 * HD]) <= 1e-2
         assert O.max_rel_err(y, y_ref) <= 1e-2
+
+
+# ---- the fused / NCCL choice of a row-parallel call is the same on every rank ----
+class _FakeComm:
+    """Stands in for awq_b200.TPComm on CPU ranks.  Its shape rule (K a multiple of 256,
+    M <= 16) makes ranks whose K differ answer differently on their own; the agreed
+    choice must still come out the same everywhere."""
+
+    def supported_shape(self, M, N, K, group_size=128):
+        return K > 0 and K % 256 == 0 and M <= 16
+
+
+def _choice_worker(rank, world, port, K, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=30))
+    try:
+        from awq_b200 import tp
+        o = _layer(K, 128, 7)
+        ro = tp.RowParallelAWQ(tp.AWQWeights(*o), world, rank, gemm=_cpu_gemm, comm=_FakeComm())
+        local = _FakeComm().supported_shape(1, 128, ro.k1 - ro.k0)
+        q.put((rank, ro.k1 - ro.k0, local, ro.fused_for(1), ro.fused_for(64)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,K,want", [
+    (2, 512, True),      # 256 rows each: every rank can run the fused kernel
+    (2, 384, False),     # 256 and 128 rows: rank 1 cannot, so neither does
+    (4, 384, False),     # 3 groups over 4 ranks: the last rank holds no rows
+])
+def test_row_parallel_fused_choice_agrees_across_ranks(world, K, want):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_choice_worker, args=(r, world, port, K, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert {g[3] for g in got} == {want}           # M = 1: one decision, the expected one
+    assert {g[4] for g in got} == {False}          # M = 64 is beyond the fused kernel
+    if not want:
+        # at least one rank would have chosen the fused kernel on its own K alone
+        assert any(g[2] for g in got) or any(g[1] == 0 for g in got)

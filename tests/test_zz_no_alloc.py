@@ -7,10 +7,12 @@ or a plugin interface that hands the library only its input and output buffers. 
 entry point keeps its split-K scratch in a 4 MiB device array inside the library.
 
 Checked here: on two calls in a row, its output matches the existing entry point
-awq_gemm_f16 (which takes a caller-allocated workspace) within the parity tolerance
-used everywhere else (max |a - b| / max |b| <= 1e-2), and a shape whose scratch would
-not fit is rejected with AWQ_ERR_WORKSPACE and a message.  This file is named so that
-pytest collects it last.
+awq_gemm_f16 (which takes a caller-allocated workspace) and the CPU oracle (the
+reference's dequantize-then-fp32-matmul restated; the two GPU entry points can run
+different kernels, so the oracle also guards against a fault they share), each within
+the parity tolerance used everywhere else (max |a - b| / max |b| <= 1e-2), and a shape
+whose scratch would not fit is rejected with AWQ_ERR_WORKSPACE and a message.  This file
+is named so that pytest collects it last.
 """
 from __future__ import annotations
 
@@ -61,13 +63,16 @@ def test_noalloc_matches_existing_entry_point(cuda, M, K, N, gs):
     dx, dqw, dqz, ds = (torch.from_numpy(np.ascontiguousarray(a)).to(cuda) for a in (x, qw, qz, s))
     ref = torch.full((M, N), float("nan"), dtype=torch.float16, device=cuda)
     assert _call_existing(lib, dx, dqw, dqz, ds, ref, gs) == 0, lib.awq_last_error()
+    oracle = O.awq_gemm_f32(x, qw, qz, s, gs)
     for _ in range(2):                                   # two calls in a row share the array
         out = torch.full((M, N), float("nan"), dtype=torch.float16, device=cuda)
         rc = _call_noalloc(lib, dx, dqw, dqz, ds, out, gs)
         assert rc == 0, lib.awq_last_error()
         torch.cuda.synchronize()
         assert torch.isfinite(out).all()
-        assert O.max_rel_err(out.float().cpu().numpy(), ref.float().cpu().numpy()) <= TOL
+        got = out.float().cpu().numpy()
+        assert O.max_rel_err(got, ref.float().cpu().numpy()) <= TOL
+        assert O.max_rel_err(got, oracle) <= TOL
 
 
 def test_noalloc_rejects_shape_beyond_its_scratch(cuda):
