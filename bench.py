@@ -15,20 +15,29 @@ with the benchmark's distributions (synthetic data; no checkpoint exists here).
             CUDA-graph replays), TB/s, whole job (max over ranks); tokens_per_s is
             1 / that step time (the linears' decode rate of the 28-layer stack)
   e2e       the same bytes / time of a step made through the public drop-in
-            ``awq_gemm_forward`` with every call's x copied from pinned host memory
-            and every output copied back inside the timed region
+            ``awq_gemm_forward``: per step one H2D copy of the step's 112 inputs from
+            pinned host memory and one D2H copy of its 112 outputs, inside the timed
+            region (wall clock, synchronised)
   roofline  decode kernel achieved GB/s vs MEASURED_PEAKS.json hbm_gbs
   prefill   M=2048 gate+up and down through the tcgen05 kernel: TFLOP/s vs the
             measured bf16 peak (fp16 and bf16 tensor rates are equal)
   cpu_baseline  the reference's dequantize-then-fp32-matmul host path (oracle port,
             torch on every host core) on one layer's 4 linears at M=1
 
+  mlp       BASELINE config 4: the Qwen2-7B MLP block (gate+up with SiLU-mul, down) at
+            M = 1 and 512 over the N GPUs (tensor parallel: gate+up by columns, down by
+            rows + all-reduce), with the row-parallel down's product alone, fused with its
+            all-reduce, and followed by NCCL, per call
+  stack     BASELINE config 5: the 28-layer linear stack with RMSNorm and residual adds
+            between the linears, a 1024-token prefill and 512 graph-replayed decode
+            steps at batch 1, tokens/s over the N GPUs
+
 With torchrun (N > 1) every rank runs the tensor-parallel stack: qkv and gate+up
-column-sharded, o and down row-sharded with an NCCL all-reduce of the fp16 output
-(strong scaling: the token's total bytes are fixed).
+column-sharded, o and down row-sharded, each row-parallel call's fp16 output summed over
+the ranks by the fused all-reduce kernel where it runs the shape, else NCCL (strong
+scaling: the token's total bytes are fixed).
 ``--impl reference`` times the reference's own CPU path (oracle port) instead.
-``--stack`` runs BASELINE config 5 instead (prefill + decode through the 28-layer linear
-stack with torch RMSNorm between the layers; see run_stack).
+``--stack`` runs only the config-5 leg (see stack_bench).
 """
 from __future__ import annotations
 
@@ -376,20 +385,30 @@ def run_ours(args):
         result["clocks"] = clk.summary()
 
     # ---- end to end through the public drop-in, host buffers ------------------------
-    hx = [torch.randn((1, K)).half().pin_memory() for (_, K, _, _, _) in calls]
-    hout = [torch.empty((1, N), dtype=torch.float16).pin_memory() for (_, _, N, _, _) in calls]
-    dx = [torch.empty((1, K), dtype=torch.float16, device=dev) for (_, K, _, _, _) in calls]
+    # Every step copies that step's inputs (one x per call) from pinned host memory in
+    # one H2D copy, makes the 112 calls through the public drop-in on device views of
+    # them, and reads every call's output back in one D2H copy (gathered on the device
+    # first); the timed region is wall clock around whole steps, synchronised.
+    x_off = [0]
+    for (_, K, _, _, _) in calls:
+        x_off.append(x_off[-1] + K)
+    hx_all = torch.randn((x_off[-1],)).half().pin_memory()
+    dx_all = torch.empty((x_off[-1],), dtype=torch.float16, device=dev)
+    dx = [dx_all[x_off[i]:x_off[i + 1]].view(1, -1) for i in range(len(calls))]
+    hout_all = torch.empty((sum(N for (_, _, N, _, _) in calls),), dtype=torch.float16).pin_memory()
 
     def e2e_step():
+        dx_all.copy_(hx_all, non_blocking=True)
+        ys = []
         for i, (name, K, N, (qw, qz, s), red) in enumerate(calls):
-            dx[i].copy_(hx[i], non_blocking=True)
             if fused[i]:
                 y = awq_b200.gemm_allreduce(dx[i], qw, qz, s, GS, comm)
             else:
                 y = awq_gemm.awq_gemm_forward(dx[i], qw, qz, s, GS)
                 if red:
                     dist.all_reduce(y)
-            hout[i].copy_(y, non_blocking=True)
+            ys.append(y.view(-1))
+        hout_all.copy_(torch.cat(ys), non_blocking=True)
         torch.cuda.synchronize()
     for _ in range(max(1, args.warmup)):
         e2e_step()
@@ -407,14 +426,23 @@ def run_ours(args):
     if rank == 0:
         result["e2e"] = {"value": round(full_bytes / (e2e_ms * 1e-3) / 1e12, 4), "unit": "TB/s",
                          "ms_per_step": round(e2e_ms, 4), "tokens_per_s": round(1e3 / e2e_ms, 1),
-                         "h2d_bytes_per_step": sum(2 * K for (_, K, _, _, _) in calls),
-                         "d2h_bytes_per_step": sum(2 * N for (_, _, N, _, _) in calls),
+                         "h2d_bytes_per_step": hx_all.numel() * hx_all.element_size(),
+                         "d2h_bytes_per_step": hout_all.numel() * hout_all.element_size(),
+                         "copies": "one H2D of the step's 112 inputs, one D2H of its 112 outputs",
+                         "host_glue": "C++ (_awq_ext)" if awq_b200._ext is not None else "ctypes",
                          "api": "kernels.awq_gemm.awq_gemm_forward (eager, 112 calls"
                                 + ((", o and down through awq_b200.gemm_allreduce: product and "
                                     "all-reduce in one kernel)" if all(
                                         f for f, c in zip(fused, calls) if c[4])
                                     else ", NCCL all-reduce after o and down)")
                                    if world > 1 else ")")}
+    calls.clear()                                      # the stack's weights: free them
+    torch.cuda.empty_cache()
+    mlp = mlp_block_bench(torch, awq_b200, dev, world, rank, comm)
+    stack = stack_bench(torch, awq_b200, dev, world, rank, comm, args)
+    if rank == 0:
+        result["mlp"] = mlp
+        result["stack"] = stack
     if world == 1:
         result["prefill"] = prefill_bench(torch, awq_b200, dev, tc_peak, peak_src, args)
         result["sweep"] = decode_sweep(torch, lib, awq_b200, dev, hbm_peak)
@@ -601,83 +629,202 @@ def run_case(args):
     print(json.dumps({"case": args.case, "reps": args.reps, "status": st}))
 
 
-def run_stack(args):
-    """BASELINE config 5 on one GPU: the 28-layer Qwen2-7B linear stack (q/k/v with bias,
-    o, gate+up, down per layer; random AWQ weights) with RMSNorm as a torch op between the
-    layers and the residual adds, a prefill of `--prefill` tokens, then `--decode` decode
-    steps at batch 1, each step one CUDA-graph replay of the 28 layers.  The drop-in's fused
-    calls are used where the reference has two kernels: the q/k/v bias in the product
-    (model/qwen2.py:108-109) and SiLU-mul with the gate+up product (:181-194).  Attention is
-    not part of the linear stack: o reads the first 3584 columns of q/k/v in its place."""
-    import torch
+def _max_over_ranks(torch, dev, world, v):
+    if world == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
 
-    import awq_b200
 
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
-    gen = torch.Generator(device=dev).manual_seed(4321)
+def _dev_time_ms(torch, dev, world, fn, reps, graph):
+    """Device time of one fn() call: `reps` calls, as one CUDA-graph replay or eagerly,
+    between CUDA events on the current stream; max over the ranks.  Every rank makes
+    the same calls (collectives included)."""
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            fn()
+        g = None
+        if graph:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                for _ in range(reps):
+                    fn()
+            g.replay()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        if graph:
+            g.replay()
+        else:
+            for _ in range(reps):
+                fn()
+        e1.record(s)
+        torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / reps
+    del g
+    return _max_over_ranks(torch, dev, world, ms)
+
+
+def mlp_block_bench(torch, awq_b200, dev, world, rank, comm):
+    """the Qwen2-7B MLP (model/qwen2.py:181-196: gate+up with SiLU-mul,
+    then down) at M = 1 and 512 over `world` GPUs through awq_b200.tp.TensorParallelMLP:
+    gate+up split by columns in whole groups, down by the matching rows, the down output
+    summed over the ranks (the fused all-reduce kernel where it runs the call, else NCCL).
+    Also, per call, the rank's down product alone, the same product fused with its
+    all-reduce, and the product followed by an NCCL all-reduce of the [M, 3584] fp16
+    output: the all-reduce's cost is the difference."""
+    import torch.distributed as dist
+
+    from awq_b200 import tp
+    gen = torch.Generator(device=dev).manual_seed(555)     # the same full weights on every rank
+    gu = tp.AWQWeights(*make_layer_dev(torch, HIDDEN, 2 * INTER, dev, gen))
+    dn = tp.AWQWeights(*make_layer_dev(torch, INTER, HIDDEN, dev, gen))
+    mlp = tp.TensorParallelMLP(gu, dn, INTER, world, rank, comm=comm if world > 1 else None)
+    del gu
+    wbytes = alg_bytes(1, HIDDEN, 2 * INTER) + alg_bytes(1, INTER, HIDDEN)
+    out = {"what": "TensorParallelMLP: gate+up (SiLU-mul fused) and down, all-reduce of the "
+                   "down output across the ranks", "n_gpus": world}
+    w = mlp.down.w
+    for M in (1, 512):
+        x = torch.randn((M, HIDDEN), device=dev, generator=gen).half()
+        graph = M <= 16                    # decode: replayed from a CUDA graph
+        ms = _dev_time_ms(torch, dev, world, lambda: mlp(x), 20 if graph else 5, graph)
+        h = torch.randn((M, mlp.inter_local), device=dev, generator=gen).half()
+        prod_ms = _dev_time_ms(torch, dev, world, lambda: awq_b200.gemm(h, w.qweight, w.qzeros,
+                                                                       w.scales, GS), 20, graph)
+        row = {"us": round(ms * 1e3, 2), "weight_TBps": round(wbytes / (ms * 1e-3) / 1e12, 3),
+               "down_product_us": round(prod_ms * 1e3, 2), "allreduce_bytes": M * HIDDEN * 2}
+        if world > 1:
+            if mlp.down.fused_for(M):
+                f_ms = _dev_time_ms(torch, dev, world, lambda: awq_b200.gemm_allreduce(
+                    h, w.qweight, w.qzeros, w.scales, GS, comm), 20, graph)
+                row["down_fused_allreduce_us"] = round(f_ms * 1e3, 2)
+                row["fused_allreduce_cost_us"] = round((f_ms - prod_ms) * 1e3, 2)
+
+            def prod_nccl():
+                y = awq_b200.gemm(h, w.qweight, w.qzeros, w.scales, GS)
+                dist.all_reduce(y)
+            n_ms = _dev_time_ms(torch, dev, world, prod_nccl, 20, False)
+            row["down_nccl_allreduce_us"] = round(n_ms * 1e3, 2)
+            row["nccl_allreduce_cost_us"] = round((n_ms - prod_ms) * 1e3, 2)
+            row["block_allreduce"] = "fused" if mlp.down.fused_for(M) else "nccl"
+        out[f"M{M}"] = row
+    st = awq_b200.device_status()
+    out["device_status"] = st
+    del mlp, dn
+    torch.cuda.empty_cache()
+    return out
+
+
+def stack_bench(torch, awq_b200, dev, world, rank, comm, args):
+    """the 28-layer Qwen2-7B linear stack (fused q/k/v with bias, o,
+    gate+up, down per layer; random AWQ weights) with RMSNorm and the residual adds as
+    torch ops between the linears, a prefill of `--prefill` tokens, then `--decode` decode
+    steps at batch 1, each one CUDA-graph replay of the 28 layers.  Over `world` GPUs the
+    attention linears are split by whole heads (AttentionLinearsTP) and the MLP by whole
+    groups (TensorParallelMLP), with the all-reduces of o and down.  The drop-in's fused
+    calls stand where the reference has two kernels: the q/k/v bias in the product
+    (model/qwen2.py:108-109) and SiLU-mul with the gate+up product (:181-194).  Attention
+    itself is not part of the linear stack: o reads the rank's query columns of q/k/v in
+    its place."""
+    from awq_b200 import tp
+    gen = torch.Generator(device=dev).manual_seed(4321)     # the same full weights everywhere
     eps = 1e-6
     layers = []
     for _ in range(LAYERS):
-        qkv = make_layer_dev(torch, HIDDEN, 4608, dev, gen)
-        qkv_b = (torch.randn(4608, device=dev, generator=gen) * 0.1).half()
-        o = make_layer_dev(torch, HIDDEN, HIDDEN, dev, gen)
-        gu = make_layer_dev(torch, HIDDEN, 2 * INTER, dev, gen)
-        dn = make_layer_dev(torch, INTER, HIDDEN, dev, gen)
+        qkv = tp.AWQWeights(*make_layer_dev(torch, HIDDEN, 4608, dev, gen),
+                            bias=(torch.randn(4608, device=dev, generator=gen) * 0.1).half())
+        o = tp.AWQWeights(*make_layer_dev(torch, HIDDEN, HIDDEN, dev, gen))
+        gu = tp.AWQWeights(*make_layer_dev(torch, HIDDEN, 2 * INTER, dev, gen))
+        dn = tp.AWQWeights(*make_layer_dev(torch, INTER, HIDDEN, dev, gen))
+        attn = tp.AttentionLinearsTP(qkv, o, 28, 4, 128, world, rank, comm=comm)
+        mlp = tp.TensorParallelMLP(gu, dn, INTER, world, rank, comm=comm)
         n1 = torch.ones(HIDDEN, dtype=torch.float16, device=dev)
         n2 = torch.ones(HIDDEN, dtype=torch.float16, device=dev)
-        layers.append((qkv, qkv_b, o, gu, dn, n1, n2))
+        layers.append((attn, mlp, n1, n2))
+        del qkv, gu
 
     def rms(h, w):
         hf = h.float()
         return (hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + eps)).half() * w
 
     def forward(h):
-        for qkv, qkv_b, o, gu, dn, n1, n2 in layers:
-            a = awq_b200.gemm(rms(h, n1), *qkv, GS, bias=qkv_b)
-            h = h + awq_b200.gemm(a[:, :HIDDEN].contiguous(), *o, GS)
-            m = awq_b200.gemm_silu_mul(rms(h, n2), *gu, GS)
-            h = h + awq_b200.gemm(m, *dn, GS)
+        for attn, mlp, n1, n2 in layers:
+            q, _, _ = attn.project_qkv(rms(h, n1))
+            h = h + attn.project_o(q.contiguous())
+            h = h + mlp(rms(h, n2))
         return h
 
     x = (torch.randn((args.prefill, HIDDEN), device=dev, generator=gen) * 0.1).half()
-    for _ in range(2):
-        forward(x)                                       # warm-up, workspaces sized
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    h = forward(x)
-    e1.record()
-    torch.cuda.synchronize()
-    prefill_ms = e0.elapsed_time(e1)
-
-    tok = h[-1:].clone()
-    for _ in range(args.warmup):
-        forward(tok)
-    torch.cuda.synchronize()
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
-        nxt = forward(tok)
-    g.replay()
-    torch.cuda.synchronize()
-    e0.record()
-    for _ in range(args.decode):
+    prefill_ms = _dev_time_ms(torch, dev, world, lambda: forward(x), 1, False)
+    tok = (torch.randn((1, HIDDEN), device=dev, generator=gen) * 0.1).half()
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            forward(tok)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            nxt = forward(tok)
         g.replay()
-        tok.copy_(nxt)                                   # the step's output feeds the next
-    e1.record()
-    torch.cuda.synchronize()
-    decode_ms = e0.elapsed_time(e1) / args.decode
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(args.decode):
+            g.replay()
+            tok.copy_(nxt)                                   # the step's output feeds the next
+        e1.record(s)
+        torch.cuda.synchronize(dev)
+    decode_ms = _max_over_ranks(torch, dev, world, e0.elapsed_time(e1) / args.decode)
     st = awq_b200.device_status()
     del g
+    layers.clear()
+    torch.cuda.empty_cache()
     w_bytes = LAYERS * sum(alg_bytes(1, K, N) for _, K, N in STACK)
-    emit_json({"metric": "Qwen2-7B AWQ linear stack, batch 1 (config 5)", "n_gpus": 1,
-               "prefill_tokens": args.prefill, "prefill_ms": round(prefill_ms, 3),
-               "prefill_tokens_per_s": round(args.prefill / prefill_ms * 1e3, 1),
-               "decode_steps": args.decode, "decode_ms_per_token": round(decode_ms, 4),
-               "decode_tokens_per_s": round(1e3 / decode_ms, 1),
-               "decode_weight_TBps": round(w_bytes / (decode_ms * 1e-3) / 1e12, 4),
-               "between_layers": "torch RMSNorm and residual adds; q/k/v bias and SiLU-mul fused",
-               "device_status": st, "data": "synthetic (random int4 AWQ weights, no checkpoint)"})
+    return {"metric": "Qwen2-7B AWQ linear stack, batch 1 (config 5)", "n_gpus": world,
+            "prefill_tokens": args.prefill, "prefill_ms": round(prefill_ms, 3),
+            "prefill_tokens_per_s": round(args.prefill / prefill_ms * 1e3, 1),
+            "decode_steps": args.decode, "decode_ms_per_token": round(decode_ms, 4),
+            "decode_tokens_per_s": round(1e3 / decode_ms, 1),
+            "decode_weight_TBps": round(w_bytes / (decode_ms * 1e-3) / 1e12, 4),
+            "between_layers": "torch RMSNorm and residual adds; q/k/v bias and SiLU-mul fused",
+            "device_status": st, "data": "synthetic (random int4 AWQ weights, no checkpoint)"}
+
+
+def run_stack(args):
+    """Only the config-5 leg (``--stack``), on one GPU or under torchrun."""
+    import torch
+    import torch.distributed as dist
+
+    import awq_b200
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    comm = None
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        comm = awq_b200.TPComm.from_group(HIDDEN)
+    res = stack_bench(torch, awq_b200, dev, world, rank, comm, args)
+    if world > 1:
+        torch.cuda.synchronize()
+        dist.barrier()
+        comm.close()
+        dist.destroy_process_group()
+    if rank == 0:
+        emit_json(res)
 
 
 def main():

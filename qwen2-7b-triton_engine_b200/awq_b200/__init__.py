@@ -10,6 +10,15 @@ Public functions
   device_status(stream)                              -> status bits of the kernels
 The reference-facing drop-in, ``kernels.awq_gemm.awq_gemm_forward``, is built on
 ``gemm``.
+
+Host glue: a decode step calls the product once per linear layer (112 times per token
+of Qwen2-7B), so the per-call host work matters.  When the C++ module ``_awq_ext``
+(``build_ext.py``, in ``lib/`` beside the library) is built, ``gemm``, ``gemm_silu_mul``
+and the drop-in's functions run their checks, output allocation, stream and workspace
+lookup in it; otherwise the same steps run here in Python and call the library through
+ctypes.  Both call the same C entry points (include/awq_b200.h) and raise the same
+exceptions.  With ``AWQ_B200_LIB`` pointing at another build of the library, only the
+ctypes path is used, so that build is the one that runs.
 """
 from __future__ import annotations
 
@@ -27,6 +36,28 @@ __all__ = ["dequant", "gemm", "gemm_silu_mul", "gemm_allreduce", "TPComm", "devi
 
 _ws_lock = threading.Lock()
 _workspaces: dict = {}
+
+
+def _load_ext():
+    """The C++ host glue, or None when it is not built (or another library is forced)."""
+    import importlib.util
+    import os
+    import sysconfig
+    default = (_lib.PKG_ROOT / "lib" / "libawq_b200.so").resolve()
+    if LIB_PATH.resolve() != default or os.environ.get("AWQ_B200_NO_EXT") == "1":
+        return None
+    path = _lib.PKG_ROOT / "lib" / ("_awq_ext" + sysconfig.get_config_var("EXT_SUFFIX"))
+    if not path.exists():
+        return None
+    _lib.load()                       # the same libawq_b200.so the module links
+    spec = importlib.util.spec_from_file_location("_awq_ext", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    mod.set_error_class(AwqError)
+    return mod
+
+
+_ext = _load_ext()
 
 
 def _require_cuda(t: torch.Tensor, name: str) -> None:
@@ -188,6 +219,8 @@ def gemm(x2d: torch.Tensor, qweight: torch.Tensor, qzeros: torch.Tensor, scales:
          out: torch.Tensor | None = None, bias: torch.Tensor | None = None) -> torch.Tensor:
     """fp16 [M, N] = x2d fp16 [M, K] @ W (+ bias fp16 [N], added in the kernel's
     epilogue before the fp16 rounding) with fp32 accumulation, on the current stream."""
+    if _ext is not None:
+        return _ext.gemm(x2d, qweight, qzeros, scales, int(group_size), int(path), out, bias)
     K, N, qweight, qzeros, scales = _prepared_weights(qweight, qzeros, scales, group_size)
     if bias is not None:
         _require_cuda(bias, "bias")
@@ -241,6 +274,8 @@ def gemm_silu_mul(x2d: torch.Tensor, qweight: torch.Tensor, qzeros: torch.Tensor
     P = x2d @ W (``awq_gemm_f16_silu_mul``): P's halves rounded to fp16, fp32
     x * sigmoid(x) * y, one fp16 rounding -- the reference MLP's awq_gemm_forward, slices
     and silu_mul_forward (model/qwen2.py:181-194) in one call."""
+    if _ext is not None:
+        return _ext.gemm_silu_mul(x2d, qweight, qzeros, scales, int(group_size), out)
     K, N, qweight, qzeros, scales = _prepared_weights(qweight, qzeros, scales, group_size)
     if N % 2:
         raise ValueError(f"N={N} is not even: no gate / up halves")

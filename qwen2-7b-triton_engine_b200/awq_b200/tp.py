@@ -193,8 +193,10 @@ class RowParallelAWQ:
 
     def fused_for(self, M: int) -> bool:
         """Whether a call with M activation rows runs the fused kernel (the same answer on
-        every rank: it depends on M, N, the group size and every rank's K only)."""
-        if self.comm is None or self.world < 2 or self.k_all is None:
+        every rank: it depends on M, N, the group size and every rank's K only).  The
+        fused kernel is the decode kernel, so it takes decode-sized calls (M <= 16); larger
+        M runs the prefill GEMM and NCCL."""
+        if self.comm is None or self.world < 2 or self.k_all is None or M > 16:
             return False
         ok = self._fused_ok.get(M)
         if ok is None:

@@ -46,6 +46,8 @@ def _dequant_to_fp16(qweight: torch.Tensor, qzeros: torch.Tensor, scales: torch.
 def awq_gemm_forward(x: torch.Tensor, qweight: torch.Tensor, qzeros: torch.Tensor,
                      scales: torch.Tensor, group_size: int = 128) -> torch.Tensor:
     """AWQ W4A16 product: ``x [..., K] fp16 @ W [K, N]`` -> fp16 ``[..., N]``."""
+    if awq_b200._ext is not None:                   # the same steps in C++ (awq_b200 docstring)
+        return awq_b200._ext.forward(x, qweight, qzeros, scales, int(group_size))
     if not isinstance(x, torch.Tensor):
         raise TypeError("x must be a torch.Tensor")
     if x.dim() < 1:
@@ -64,6 +66,8 @@ def awq_gemm_bias_forward(x: torch.Tensor, qweight: torch.Tensor, qzeros: torch.
     the product's epilogue.  For the reference's biased call sites, which add the bias
     after the product (``model/qwen2.py:45-46``, ``:108-109``).  Not in the reference
     module; the result differs from the two-step form only by its single fp16 rounding."""
+    if awq_b200._ext is not None:
+        return awq_b200._ext.forward_bias(x, qweight, qzeros, scales, bias, int(group_size))
     if not isinstance(x, torch.Tensor):
         raise TypeError("x must be a torch.Tensor")
     if x.dim() < 1:
@@ -80,6 +84,8 @@ def awq_gemm_silu_mul_forward(x: torch.Tensor, qweight: torch.Tensor, qzeros: to
     """``silu(P[..., :N/2]) * P[..., N/2:]`` for ``P = awq_gemm_forward(x, ...)`` with the
     fused gate+up weights (N = 2 * intermediate): the MLP activation of the reference
     (``model/qwen2.py:181-194``) in one call; up to 8 tokens P is never written."""
+    if awq_b200._ext is not None:
+        return awq_b200._ext.forward_silu_mul(x, qweight, qzeros, scales, int(group_size))
     if not isinstance(x, torch.Tensor):
         raise TypeError("x must be a torch.Tensor")
     if x.dim() < 1:
