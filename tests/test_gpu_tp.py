@@ -246,3 +246,84 @@ def test_fused_allreduce_world2_matches_single_gpu_and_ranks_agree(cuda):
         assert st == 0
         assert np.array_equal(eager, graphed)
     assert np.array_equal(got[0][1], got[1][1])
+
+
+def _recovery_worker(rank, world, port, seed, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    import datetime
+    import sys
+    sys.path.insert(0, os.environ["AWQ_PKG"])
+    sys.path.insert(0, os.environ["AWQ_REPO"])
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60), device_id=dev)
+    comm = None
+    try:
+        import awq_b200
+        from awq_b200 import tp
+        comm = awq_b200.TPComm.from_group(HIDDEN)
+        comm.set_timeout(0.3)
+        _, _, o = _layers(seed)
+        to = lambda t: tuple(torch.from_numpy(np.ascontiguousarray(a)).to(dev) for a in t)
+        ro = tp.RowParallelAWQ(tp.AWQWeights(*to(o)), world, rank, comm=comm)
+        x = torch.from_numpy(O.make_x(1, HIDDEN, seed=seed + 3)).to(dev)
+        xl = x[:, ro.k0:ro.k1].contiguous()
+        assert ro.fused_for(1)
+        if rank == 0:
+            ro(xl)            # rank 1 skips this call: rank 0's wait for its tiles runs out
+        torch.cuda.synchronize()
+        raised = ""
+        try:
+            comm.check(collective=True)    # both ranks learn of it, not only rank 0
+        except awq_b200.AwqError as e:
+            raised = str(e)
+        comm.reset()                       # collective: barrier, clear, barrier
+        z = ro(xl)                         # the next call is correct again
+        torch.cuda.synchronize()
+        q.put((rank, raised, z.cpu().numpy(), awq_b200.device_status()))
+    except BaseException:
+        import traceback
+        q.put(("error", rank, traceback.format_exc()))
+        raise
+    finally:
+        torch.cuda.synchronize()
+        if comm is not None:
+            dist.barrier()
+            comm.close()
+        dist.destroy_process_group()
+
+
+def test_fused_allreduce_recovers_after_a_skipped_call(cuda):
+    """A rank that skips a fused row-parallel call leaves the other rank's wait to run out
+    (bounded: status bit 4, no hang).  A collective ``TPComm.check`` raises AwqError on
+    both ranks, ``TPComm.reset`` clears both communicators, and the next fused call gives
+    the single-GPU product, bit-identical on both ranks."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import awq_b200
+    from conftest import PKG, REPO
+    world, seed = 2, 41
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    os.environ.update(AWQ_PKG=str(PKG), AWQ_REPO=str(REPO))
+    port = _free_port()
+    procs = [ctx.Process(target=_recovery_worker, args=(r, world, port, seed, q)) for r in range(world)]
+    _start(procs, world)
+    got = {rank: (raised, z, st) for rank, raised, z, st in _collect(q, procs, world)}
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    _, _, o = _layers(seed)
+    to = lambda t: tuple(torch.from_numpy(np.ascontiguousarray(a)).to(cuda) for a in t)
+    x = torch.from_numpy(O.make_x(1, HIDDEN, seed=seed + 3)).to(cuda)
+    z_ref = awq_b200.gemm(x, *to(o), 128).float().cpu().numpy()
+    for rank in range(world):
+        raised, z, st = got[rank]
+        assert "timed out waiting for another rank" in raised, (rank, raised)
+        assert st == 0
+        assert O.max_rel_err(z.astype(np.float32), z_ref) <= TOL, rank
+    assert np.array_equal(got[0][1], got[1][1])
