@@ -30,6 +30,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "awq_common.cuh"
@@ -67,8 +68,9 @@ struct Geo {
   static constexpr uint32_t T_STAGE = (T_ZR + ZR_BYTES + 1023) / 1024 * 1024;
   static constexpr uint32_t OFF_T = 0;
   static constexpr uint32_t OFF_B = OFF_T + TSTAGES * T_STAGE;
-  static constexpr uint32_t OFF_BAR = OFF_B + BSTAGES * B_BYTES;  // tfull, tempty, bfull, bempty, accf
-  static constexpr uint32_t NBARS = 2 * TSTAGES + 2 * BSTAGES + 1;
+  // tfull, tempty, bfull, bempty, accf, tmem empty, drain
+  static constexpr uint32_t OFF_BAR = OFF_B + BSTAGES * B_BYTES;
+  static constexpr uint32_t NBARS = 2 * TSTAGES + 2 * BSTAGES + 3;
   static constexpr uint32_t OFF_MISC = OFF_BAR + NBARS * 8;
   static constexpr uint32_t SMEM_BYTES = OFF_MISC + 16 + 1024;      // + alignment slack
   static constexpr uint32_t TMEM_COLS = 256 * NACC;
@@ -82,7 +84,68 @@ struct TcArgs {
   const __half* bias;   // fp16 [N] added to every output row in fp32, or null
   int splits;           // CTAs along K per output tile (blockIdx.z); > 1: fp32 partials
   float* part;          // [splits][M][N] fp32 partials when splits > 1
+  // stream-K (streamk != 0, splits == 1; tiles < gridDim.x): CTA c < tiles runs K steps
+  // [0, sk_split) of tile c -- those CTAs move through K together, as one tile-per-CTA wave
+  // does, so each x and weight slab is fetched from HBM once and read from L2 by the other
+  // tiles of its row or column.  The other gridDim.x - tiles CTAs share the tiles' last
+  // K/64 - sk_split steps evenly in linear (tile, step) order.  The last CTA to finish a
+  // part of a tile sums the tile from fp32 slots.
+  int streamk;
+  int tiles_n;
+  int sk_tiles;
+  int sk_split;
+  float* sk_part;       // [tiles][kSkSlots][BM * 256] fp32, each slot in fragment order
+  int* sk_cnt;          // per-tile arrivals, zero between calls
 };
+
+constexpr int kSkSlots = 3;   // CTAs per tile under stream-K, at most (the tail's sharers <= 2)
+constexpr int kMaxSeg = 8;    // tiles a CTA works on under stream-K, at most
+
+// One tile's part of a CTA's work: K steps [k0, k1) of tile (tile_m, tile_n), the idx-th
+// of the n CTAs that work on the tile.
+struct TcSeg {
+  int tile_m, tile_n, k0, k1, idx, n;
+};
+
+// Writes one warp's 32 rows x 32 columns of fp16 results (`h`: this lane's row, 16 packed
+// pairs) through 2 KB of shared memory at `stage`, so that each global store covers 8 rows
+// x 64 contiguous bytes instead of 32 rows x 16 bytes.  The 16-byte chunks of a row are
+// XOR-swizzled by (row / 2) % 4, which keeps both the row-wise writes and the chunk-wise
+// reads free of bank conflicts.  Rows at or past M are not stored.
+__device__ __forceinline__ void store_rows_staged(uint32_t stage, const uint32_t (&h)[16],
+                                                  __half* out, int64_t ldo, int row0, int col,
+                                                  int M, int lane) {
+  const uint32_t sw = (uint32_t)(lane >> 1) & 3u;
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    sm100::st_shared_v4(stage + (uint32_t)lane * 64u + (((uint32_t)j ^ sw) << 4), h[4 * j],
+                        h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
+  __syncwarp();
+  const int ch = lane & 3;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = i * 8 + (lane >> 2);
+    const uint4 v = sm100::ld_shared_v4(stage + (uint32_t)r * 64u +
+                                        (((uint32_t)ch ^ ((uint32_t)(r >> 1) & 3u)) << 4));
+    if (row0 + r < M)
+      *reinterpret_cast<uint4*>(out + (int64_t)(row0 + r) * ldo + col + ch * 8) = v;
+  }
+  __syncwarp();
+}
+
+__device__ __forceinline__ void epi_bar_sync() {       // the 8 dequant / epilogue warps
+  asm volatile("bar.sync 1, %0;" ::"n"(kDeqWarps * 32) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
 
 template <int NACC>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -102,19 +165,66 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int tile_m = blockIdx.x, tile_n = blockIdx.y;
-  // this CTA's K steps [kt0, kt0 + KT) (split-K over blockIdx.z; the ranges of one tile
-  // differ by at most one step); the rings below count steps from 0 within the range
+  // this CTA's work as segments (tile, K steps).  Tile grid: the tile of (blockIdx.x,
+  // blockIdx.y), K steps split over blockIdx.z (the ranges of one tile differ by at most
+  // one step).  Stream-K: CTA c < tiles takes steps [0, S) of tile c (slot 0); CTA
+  // tiles + j of the G2 = gridDim.x - tiles others takes linear steps
+  // [j TT / G2, (j + 1) TT / G2) of the tails, TT = tiles x L with L = K/64 - S, step u
+  // being step S + u % L of tile u / L (slots 1 and 2 of a tile: its tail's first and
+  // second sharer).  The rings below count the CTA's steps from 0 across its segments.
   const int kt_all = args.K / BK;
-  const int kt0 = (int)((int64_t)blockIdx.z * kt_all / args.splits);
-  const int KT = (int)((int64_t)(blockIdx.z + 1) * kt_all / args.splits) - kt0;
+  TcSeg seg[kMaxSeg];
+  int nseg = 0;
+  if (!args.streamk) {
+    const int kt0 = (int)((int64_t)blockIdx.z * kt_all / args.splits);
+    const int kt1 = (int)((int64_t)(blockIdx.z + 1) * kt_all / args.splits);
+    seg[0] = TcSeg{(int)blockIdx.x, (int)blockIdx.y, kt0, kt1, (int)blockIdx.z, args.splits};
+    nseg = 1;
+  } else {
+    const int T = args.sk_tiles, S = args.sk_split, L = kt_all - S;
+    const int64_t G2 = (int64_t)gridDim.x - T, TT = (int64_t)T * L;
+    auto start = [&](int64_t j) { return j * TT / G2; };
+    auto cta_of = [&](int64_t u) {                    // the sharer whose range holds step u
+      int64_t j = u * G2 / TT;
+      if (j + 1 < G2 && start(j + 1) <= u) ++j;
+      return j;
+    };
+    const int c = blockIdx.x;
+    if (c < T) {
+      const int64_t jf = cta_of((int64_t)c * L), jl = cta_of((int64_t)c * L + L - 1);
+      seg[nseg++] = TcSeg{c / args.tiles_n, c % args.tiles_n, 0, S, 0, (int)(jl - jf) + 2};
+    } else {
+      const int64_t j = c - T, u1 = start(j + 1);
+      int64_t u = start(j);
+      for (; u < u1 && nseg < kMaxSeg;) {
+        const int64_t t = u / L, tb = t * L;
+        const int64_t e = u1 < tb + L ? u1 : tb + L;
+        const int64_t jf = cta_of(tb), jl = cta_of(tb + L - 1);
+        seg[nseg++] = TcSeg{(int)(t / args.tiles_n), (int)(t % args.tiles_n), S + (int)(u - tb),
+                            S + (int)(e - tb), (int)(j - jf) + 1, (int)(jl - jf) + 2};
+        u = e;
+      }
+      // the host keeps every share within kMaxSeg tiles and each tail within two sharers;
+      // a launch outside that reports a shape error rather than drop steps
+      if (u < u1 && tid == 0) atomicOr(args.status, kDevErrShape);
+    }
+    for (int si = 0; si < nseg; ++si)
+      if (seg[si].n > kSkSlots) {
+        if (tid == 0) atomicOr(args.status, kDevErrShape);
+        nseg = 0;
+      }
+  }
 
   auto bar_tfull = [&](int s) { return sbase + OFF_BAR + 8u * s; };
   auto bar_tempty = [&](int s) { return sbase + OFF_BAR + 8u * (TSTAGES + s); };
   auto bar_bfull = [&](int s) { return sbase + OFF_BAR + 8u * (2 * TSTAGES + s); };
   auto bar_bempty = [&](int s) { return sbase + OFF_BAR + 8u * (2 * TSTAGES + BSTAGES + s); };
   const uint32_t bar_accf = sbase + OFF_BAR + 8u * (2 * TSTAGES + 2 * BSTAGES);
+  const uint32_t bar_tmem_empty = bar_accf + 8u;   // epilogue read the accumulator (stream-K)
+  const uint32_t bar_drain = bar_accf + 16u;       // every MMA of this CTA completed
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(sgen + OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sgen + OFF_MISC + 4);
+  volatile int* last_flag = reinterpret_cast<volatile int*>(sgen + OFF_MISC + 8);
 
   if (tid == 0) {
     for (int s = 0; s < TSTAGES; ++s) {
@@ -126,6 +236,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       sm100::mbar_init(bar_bempty(s), 1);
     }
     sm100::mbar_init(bar_accf, 1);
+    sm100::mbar_init(bar_tmem_empty, 1);
+    sm100::mbar_init(bar_drain, 1);
     sm100::fence_mbar_init();
     *abort_flag = 0;
     sm100::prefetch_tmap(&tmA);
@@ -145,55 +257,67 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   if (warp == 0) {
     // ------------------------------------------------------------- TMA producer ----
     if (lane == 0) {
-      int kt = 0;
-      for (; kt < KT; ++kt) {
-        const int s = kt % TSTAGES;
-        if (kt >= TSTAGES &&
-            !sm100::mbar_wait_bounded(bar_tempty(s), ((kt / TSTAGES) & 1) ^ 1, args.status)) {
-          *abort_flag = 1;
-          break;
+      int j = 0;                                 // the CTA's step counter (ring position)
+      for (int si = 0; si < nseg && !*abort_flag; ++si) {
+        const TcSeg& sg = seg[si];
+        for (int kt = sg.k0; kt < sg.k1; ++kt, ++j) {
+          const int s = j % TSTAGES;
+          if (j >= TSTAGES &&
+              !sm100::mbar_wait_bounded(bar_tempty(s), ((j / TSTAGES) & 1) ^ 1, args.status)) {
+            *abort_flag = 1;
+            break;
+          }
+          if (*abort_flag) break;
+          const int k0 = kt * BK;
+          const int grp = k0 / args.gs;
+          const uint32_t st = sbase + OFF_T + s * T_STAGE;
+          sm100::mbar_arrive_expect_tx(bar_tfull(s), TX_BYTES);
+          sm100::tma_load_2d(st, &tmA, bar_tfull(s), k0, sg.tile_m * BM);
+          sm100::tma_load_2d(st + T_RAW, &tmW, bar_tfull(s), sg.tile_n * (BN / 8), k0);
+          sm100::tma_load_2d(st + T_SC, &tmS, bar_tfull(s), sg.tile_n * BN, grp);
+          sm100::tma_load_2d(st + T_ZR, &tmZ, bar_tfull(s), sg.tile_n * (BN / 8), grp);
         }
-        if (*abort_flag) break;
-        const int k0 = (kt0 + kt) * BK;
-        const int grp = k0 / args.gs;
-        const uint32_t st = sbase + OFF_T + s * T_STAGE;
-        sm100::mbar_arrive_expect_tx(bar_tfull(s), TX_BYTES);
-        sm100::tma_load_2d(st, &tmA, bar_tfull(s), k0, tile_m * BM);
-        sm100::tma_load_2d(st + T_RAW, &tmW, bar_tfull(s), tile_n * (BN / 8), k0);
-        sm100::tma_load_2d(st + T_SC, &tmS, bar_tfull(s), tile_n * BN, grp);
-        sm100::tma_load_2d(st + T_ZR, &tmZ, bar_tfull(s), tile_n * (BN / 8), grp);
       }
       // drain: the copies of the last (up to) TSTAGES steps must land before exit
-      for (int j = (kt > TSTAGES ? kt - TSTAGES : 0); j < kt; ++j)
-        sm100::mbar_wait_bounded(bar_tfull(j % TSTAGES), (j / TSTAGES) & 1, args.status);
+      for (int i = (j > TSTAGES ? j - TSTAGES : 0); i < j; ++i)
+        sm100::mbar_wait_bounded(bar_tfull(i % TSTAGES), (i / TSTAGES) & 1, args.status);
     }
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------- MMA issuer ------
     if (lane == 0) {
-      for (int kt = 0; kt < KT; ++kt) {
-        const int ts = kt % TSTAGES, bs = kt % BSTAGES;
-        if (!sm100::mbar_wait_bounded(bar_bfull(bs), (kt / BSTAGES) & 1, args.status)) {
-          *abort_flag = 1;
-          break;
+      int j = 0;
+      for (int si = 0; si < nseg; ++si) {
+        const TcSeg& sg = seg[si];
+        // a second segment reuses the accumulator: wait until the epilogue has read it
+        if (si > 0) {
+          if (!sm100::mbar_wait_bounded(bar_tmem_empty, (si - 1) & 1, args.status)) *abort_flag = 1;
+          sm100::tc_fence_after();
         }
-        if (*abort_flag) break;
-        sm100::tc_fence_after();
-        const uint32_t a0 = sbase + OFF_T + ts * T_STAGE;
-        const uint32_t b0 = sbase + OFF_B + bs * B_BYTES;
-#pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk) {
-          const uint64_t bd = sm100::umma_desc_sw128(b0 + kk * 2 * B_SBO, B_LBO, B_SBO);
-#pragma unroll
-          for (int h = 0; h < NACC; ++h) {     // rows [128 h, 128 h + 128) -> TMEM cols 256 h
-            const uint64_t ad = sm100::umma_desc_sw128(a0 + h * 128 * 128 + kk * 32, 16, A_SBO);
-            sm100::umma_f16(tmem_d + 256 * h, ad, bd, kIdesc, (kt | kk) != 0);
+        for (int kt = sg.k0; kt < sg.k1 && !*abort_flag; ++kt, ++j) {
+          const int ts = j % TSTAGES, bs = j % BSTAGES;
+          if (!sm100::mbar_wait_bounded(bar_bfull(bs), (j / BSTAGES) & 1, args.status)) {
+            *abort_flag = 1;
+            break;
           }
+          if (*abort_flag) break;
+          sm100::tc_fence_after();
+          const uint32_t a0 = sbase + OFF_T + ts * T_STAGE;
+          const uint32_t b0 = sbase + OFF_B + bs * B_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t bd = sm100::umma_desc_sw128(b0 + kk * 2 * B_SBO, B_LBO, B_SBO);
+#pragma unroll
+            for (int h = 0; h < NACC; ++h) {   // rows [128 h, 128 h + 128) -> TMEM cols 256 h
+              const uint64_t ad = sm100::umma_desc_sw128(a0 + h * 128 * 128 + kk * 32, 16, A_SBO);
+              sm100::umma_f16(tmem_d + 256 * h, ad, bd, kIdesc, (kt != sg.k0 || kk != 0) ? 1u : 0u);
+            }
+          }
+          sm100::umma_commit(bar_tempty(ts));    // x tile and packed inputs consumed
+          sm100::umma_commit(bar_bempty(bs));    // dequantized B consumed
         }
-        sm100::umma_commit(bar_tempty(ts));      // x tile and packed inputs consumed
-        sm100::umma_commit(bar_bempty(bs));      // dequantized B consumed
+        sm100::umma_commit(bar_accf);            // phase si: the segment's MMAs have completed
       }
-      sm100::umma_commit(bar_accf);              // arrives when every issued MMA has completed
     }
     __syncwarp();
   } else {
@@ -201,81 +325,196 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const int dw = warp - 2;                 // 0..7: rows [8 dw, 8 dw + 8) of a K step
     const int w = lane;                      // packed word column within the tile
     const uint32_t bst_lane = (uint32_t)(w >> 3) * B_LBO + (uint32_t)dw * B_SBO;
-    for (int kt = 0; kt < KT; ++kt) {
-      const int ts = kt % TSTAGES, bs = kt % BSTAGES;
-      if (!sm100::mbar_wait_bounded(bar_tfull(ts), (kt / TSTAGES) & 1, args.status)) {
-        *abort_flag = 1;
-        break;
-      }
-      if (kt >= BSTAGES &&
-          !sm100::mbar_wait_bounded(bar_bempty(bs), ((kt / BSTAGES) & 1) ^ 1, args.status)) {
-        *abort_flag = 1;
-        break;
-      }
-      if (*abort_flag) break;
-      const unsigned char* tst = sgen + OFF_T + ts * T_STAGE;
-      const uint32_t* raw = reinterpret_cast<const uint32_t*>(tst + T_RAW) + dw * 8 * (BN / 8);
-      const uint32_t zw = reinterpret_cast<const uint32_t*>(tst + T_ZR)[w];
-      const uint4 s4 = reinterpret_cast<const uint4*>(tst + T_SC)[w];
-      uint32_t zc[4], sc[4] = {s4.x, s4.y, s4.z, s4.w};
-      zero_consts(zw, zc);
-      uint32_t wv[8];
+    int j = 0;
+    for (int si = 0; si < nseg; ++si) {
+      const TcSeg& sg = seg[si];
+      for (int kt = sg.k0; kt < sg.k1 && !*abort_flag; ++kt, ++j) {
+        const int ts = j % TSTAGES, bs = j % BSTAGES;
+        if (!sm100::mbar_wait_bounded(bar_tfull(ts), (j / TSTAGES) & 1, args.status)) {
+          *abort_flag = 1;
+          break;
+        }
+        if (j >= BSTAGES &&
+            !sm100::mbar_wait_bounded(bar_bempty(bs), ((j / BSTAGES) & 1) ^ 1, args.status)) {
+          *abort_flag = 1;
+          break;
+        }
+        if (*abort_flag) break;
+        const unsigned char* tst = sgen + OFF_T + ts * T_STAGE;
+        const uint32_t* raw = reinterpret_cast<const uint32_t*>(tst + T_RAW) + dw * 8 * (BN / 8);
+        const uint32_t zw = reinterpret_cast<const uint32_t*>(tst + T_ZR)[w];
+        const uint4 s4 = reinterpret_cast<const uint4*>(tst + T_SC)[w];
+        uint32_t zc[4], sc[4] = {s4.x, s4.y, s4.z, s4.w};
+        zero_consts(zw, zc);
+        uint32_t wv[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) wv[i] = raw[i * (BN / 8) + w];
-      const uint32_t bstage = sbase + OFF_B + bs * B_BYTES + bst_lane;
+        for (int i = 0; i < 8; ++i) wv[i] = raw[i * (BN / 8) + w];
+        const uint32_t bstage = sbase + OFF_B + bs * B_BYTES + bst_lane;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        uint32_t d[4];
-        dequant_word(wv[i], zc, sc, d);
-        const uint32_t addr = bstage + (uint32_t)i * 128u + ((uint32_t)((w & 7) ^ i) << 4);
-        sm100::st_shared_v4(addr, d[0], d[1], d[2], d[3]);
+        for (int i = 0; i < 8; ++i) {
+          uint32_t d[4];
+          dequant_word(wv[i], zc, sc, d);
+          const uint32_t addr = bstage + (uint32_t)i * 128u + ((uint32_t)((w & 7) ^ i) << 4);
+          sm100::st_shared_v4(addr, d[0], d[1], d[2], d[3]);
+        }
+        sm100::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) sm100::mbar_arrive(bar_bfull(bs));
       }
-      sm100::fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) sm100::mbar_arrive(bar_bfull(bs));
-    }
 
-    // ------------------------------------------------------------- epilogue --------
-    const bool ok = sm100::mbar_wait_bounded(bar_accf, 0, args.status);
-    sm100::tc_fence_after();
-    if (ok && !*abort_flag) {
+      // ----------------------------------------------------------- epilogue --------
+      // the segment's accumulator: phase si of the accumulator barrier
+      const bool ok = sm100::mbar_wait_bounded(bar_accf, si & 1, args.status);
+      sm100::tc_fence_after();
       const int q = warp & 3;                  // TMEM lane quarter this warp may access
       const int half = dw >> 2;                // the two warps of a quarter split the work
       // NACC == 1: split the 256 columns; NACC == 2: one accumulator (128 rows) each
       const int acc = NACC == 2 ? half : 0;
       const int c_lo = NACC == 2 ? 0 : half * 4, c_hi = NACC == 2 ? 8 : half * 4 + 4;
-      const int row = tile_m * BM + acc * 128 + q * 32 + lane;
+      const int rloc = acc * 128 + q * 32 + lane;   // row within the tile
+      const int row = sg.tile_m * BM + rloc;
       const uint32_t taddr = tmem_d + acc * 256 + ((uint32_t)(q * 32) << 16);
+      // stream-K: a tile shared by several CTAs leaves this CTA as an fp32 partial in the
+      // tile's slot sg.idx; the last CTA to arrive sums the slots
+      const bool shared_tile = args.streamk && sg.n > 1;
+      const int tile = sg.tile_m * args.tiles_n + sg.tile_n;
+      float* slot = shared_tile ? args.sk_part + ((size_t)tile * kSkSlots + sg.idx) * BM * BN
+                                : nullptr;
+      // fp16 results leave through 2 KB of shared memory per warp in B stage 0: every MMA
+      // of this CTA so far has completed (the accumulator barrier), so no MMA reads it
+      const uint32_t stage = sbase + OFF_B + (uint32_t)dw * 2048u;
+      const int row0 = sg.tile_m * BM + acc * 128 + q * 32;
+      const bool live = ok && !*abort_flag;
+      if (!shared_tile) {
+        if (live) {
 #pragma unroll 1
-      for (int c = c_lo; c < c_hi; ++c) {
-        uint32_t v[32];
-        sm100::tmem_ld_32x32b_x32(taddr + c * 32, v);
-        sm100::tmem_ld_wait();
-        const int col = tile_n * BN + c * 32;
-        if (row < args.M && col < args.N && args.splits > 1) {
-          // split-K: this CTA's fp32 partial, summed (with the bias) by the reduce kernel
-          float4* dst = reinterpret_cast<float4*>(
-              args.part + ((size_t)blockIdx.z * args.M + row) * args.N + col);
+          for (int c = c_lo; c < c_hi; ++c) {
+            uint32_t v[32];
+            sm100::tmem_ld_32x32b_x32(taddr + c * 32, v);
+            sm100::tmem_ld_wait();
+            const int col = sg.tile_n * BN + c * 32;
+            if (col >= args.N) continue;         // the same for the whole warp
+            if (args.splits > 1) {
+              // the split-K plane, summed with the bias by the reduce kernel
+              if (row >= args.M) continue;
+              float4* dst = reinterpret_cast<float4*>(
+                  args.part + ((size_t)blockIdx.z * args.M + row) * args.N + col);
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
-            dst[j] = make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
-                                 __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
-        } else if (row < args.M && col < args.N) {
-          if (args.bias) {                      // the columns' bias, added in fp32
+              for (int jj = 0; jj < 8; ++jj)
+                dst[jj] = make_float4(__uint_as_float(v[4 * jj]), __uint_as_float(v[4 * jj + 1]),
+                                      __uint_as_float(v[4 * jj + 2]), __uint_as_float(v[4 * jj + 3]));
+            } else {
+              if (args.bias) {                  // the columns' bias, added in fp32
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              v[j] = __float_as_uint(__uint_as_float(v[j]) + __half2float(args.bias[col + j]));
+                for (int jj = 0; jj < 32; ++jj)
+                  v[jj] = __float_as_uint(__uint_as_float(v[jj]) + __half2float(args.bias[col + jj]));
+              }
+              uint32_t h[16];
+#pragma unroll
+              for (int jj = 0; jj < 16; ++jj)
+                h[jj] = h2_as_u32(__floats2half2_rn(__uint_as_float(v[2 * jj]), __uint_as_float(v[2 * jj + 1])));
+              store_rows_staged(stage, h, args.out, args.ldo, row0, col, args.M, lane);
+            }
           }
-          uint32_t h[16];
+        }
+      } else {
+        // A part of a shared tile.  If the tile's other n - 1 parts are already in their
+        // slots (an acquire load of the tile's counter), this CTA sums the tile at once and
+        // never writes its own slot.  Otherwise it writes its slot (fp32, fragment order:
+        // float4 (c * 8 + jj) of row rloc at (c * 8 + jj) * BM + rloc, so a warp's store
+        // covers 512 contiguous bytes) and takes a ticket (acq_rel, gpu scope; its release
+        // covers the slot stores the barrier ordered before it); the last ticket sums.  The
+        // sum runs in slot order -- the same bits whichever CTA makes it -- with this CTA's
+        // own part read back from TMEM, then adds the bias, writes fp16 and clears the
+        // counter for the next call.
+        if (dw == 0 && lane == 0) *last_flag = ld_acquire_gpu(args.sk_cnt + tile) == sg.n - 1 ? 1 : 0;
+        epi_bar_sync();
+        if (!*last_flag) {
+          if (live) {
+#pragma unroll 1
+            for (int c = c_lo; c < c_hi; ++c) {
+              uint32_t v[32];
+              sm100::tmem_ld_32x32b_x32(taddr + c * 32, v);
+              sm100::tmem_ld_wait();
+              float4* dst = reinterpret_cast<float4*>(slot) + (size_t)c * 8 * BM + rloc;
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
-            h[j] = h2_as_u32(__floats2half2_rn(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1])));
-          uint4* dst = reinterpret_cast<uint4*>(args.out + (int64_t)row * args.ldo + col);
+              for (int jj = 0; jj < 8; ++jj)
+                dst[(size_t)jj * BM] = make_float4(__uint_as_float(v[4 * jj]), __uint_as_float(v[4 * jj + 1]),
+                                                   __uint_as_float(v[4 * jj + 2]), __uint_as_float(v[4 * jj + 3]));
+            }
+          }
+          epi_bar_sync();
+          if (dw == 0 && lane == 0)
+            *last_flag = (atom_add_acq_rel_gpu(args.sk_cnt + tile, 1) == sg.n - 1) ? 1 : 0;
+          epi_bar_sync();
+        }
+        if (*last_flag) {
+          if (live) {
+            // the other parts' slots: o0 < o1 (o1 < 0 when the tile has two parts).  Each
+            // round has 16 float4 loads per thread in flight: two chunks of the one other
+            // slot, or one chunk of both.
+            const int o0 = sg.idx == 0 ? 1 : 0;
+            const int o1 = sg.n < 3 ? -1 : (sg.idx == 2 ? 1 : 2);
+            const bool two = o1 < 0;
+            const float4* tbase =
+                reinterpret_cast<const float4*>(args.sk_part + (size_t)tile * kSkSlots * BM * BN) + rloc;
+#pragma unroll 1
+            for (int c = c_lo; c < c_hi; c += two ? 2 : 1) {
+              const float4* s0 = tbase + (size_t)o0 * (BM * BN / 4) + (size_t)c * 8 * BM;
+              const float4* s1 = two ? s0 + (size_t)8 * BM
+                                     : tbase + (size_t)o1 * (BM * BN / 4) + (size_t)c * 8 * BM;
+              float4 p0[8], p1[8];
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            dst[j] = make_uint4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
+              for (int jj = 0; jj < 8; ++jj) {
+                p0[jj] = __ldcg(s0 + (size_t)jj * BM);
+                p1[jj] = __ldcg(s1 + (size_t)jj * BM);
+              }
+#pragma unroll 1
+              for (int k = 0; k < (two ? 2 : 1); ++k) {
+                const int cc = c + k;
+                const int col = sg.tile_n * BN + cc * 32;
+                if (col >= args.N) continue;     // the same for the whole warp
+                uint32_t v[32];
+                sm100::tmem_ld_32x32b_x32(taddr + cc * 32, v);
+                sm100::tmem_ld_wait();
+                float sum[32];
+#pragma unroll
+                for (int jj = 0; jj < 8; ++jj) {
+                  const float4 f0 = (two && k == 1) ? p1[jj] : p0[jj];
+                  const float4 f1 = p1[jj];
+                  const float own[4] = {__uint_as_float(v[4 * jj]), __uint_as_float(v[4 * jj + 1]),
+                                        __uint_as_float(v[4 * jj + 2]), __uint_as_float(v[4 * jj + 3])};
+                  const float a0[4] = {f0.x, f0.y, f0.z, f0.w}, a1[4] = {f1.x, f1.y, f1.z, f1.w};
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) {
+                    // parts in slot order 0, 1, 2 from 0.0f: own part at sg.idx, then the
+                    // other slots o0 (a0) and o1 (a1) in their places
+                    float acc = 0.f;
+                    acc += sg.idx == 0 ? own[e] : a0[e];
+                    acc += sg.idx == 1 ? own[e] : (sg.idx == 0 ? a0[e] : a1[e]);
+                    if (!two) acc += sg.idx == 2 ? own[e] : a1[e];
+                    sum[4 * jj + e] = acc;
+                  }
+                }
+                if (args.bias) {
+#pragma unroll
+                  for (int jj = 0; jj < 32; ++jj) sum[jj] += __half2float(args.bias[col + jj]);
+                }
+                uint32_t h[16];
+#pragma unroll
+                for (int jj = 0; jj < 16; ++jj) h[jj] = h2_as_u32(__floats2half2_rn(sum[2 * jj], sum[2 * jj + 1]));
+                store_rows_staged(stage, h, args.out, args.ldo, row0, col, args.M, lane);
+              }
+            }
+          }
+          if (dw == 0 && lane == 0) args.sk_cnt[tile] = 0;   // ready for the next call
         }
       }
+      // every epilogue thread has read the accumulator and left the staging area (B stage
+      // 0, which the next segment's dequant writes)
+      sm100::tc_fence_before();
+      epi_bar_sync();
+      if (si + 1 < nseg && dw == 0 && lane == 0) sm100::mbar_arrive(bar_tmem_empty);
     }
   }
 
@@ -283,9 +522,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   __syncthreads();
   if (warp == 1) {
     __syncwarp();
-    // in the abort path the accumulator commit may still be in flight: wait for it
-    // (bounded) before giving the columns back
-    if (*abort_flag) sm100::mbar_wait_bounded(bar_accf, 0, nullptr, 100000000ull);
+    // every MMA this CTA issued has completed (in the abort path some may still be in
+    // flight) before the columns go back: one more commit, bounded wait
+    if (lane == 0) {
+      sm100::umma_commit(bar_drain);
+      sm100::mbar_wait_bounded(bar_drain, 0, nullptr, 100000000ull);
+    }
+    __syncwarp();
     sm100::tc_fence_after();
     sm100::tmem_dealloc(tmem_d, TMEM_COLS);
   }
@@ -652,9 +895,51 @@ int tc_splits(int64_t M, int64_t N, int64_t K, int num_sms) {
   return s < 1 ? 1 : (int)s;
 }
 
+// Stream-K schedule of the tcgen05 kernel, for output tiles that fill between half and
+// most of one wave (down at M = 2048: 8 x 14 = 112 tiles on 148 SMs).  One CTA per tile
+// runs the first S K steps; the other num_sms - tiles CTAs share the tiles' last K/64 - S
+// steps evenly.  Every share is at least one tail long, so a tile has at most three parts
+// (kSkSlots), and reaches at most kMaxSeg tiles.  Costs in K steps, from per-CTA timelines
+// on B200 (a K step of a 256 x 256 tile takes ~0.85 us): a share pays kSkSegCost for each
+// further tile it reaches (its 256 KB fp32 slot written while the other SMs stream their
+// inputs: ~6.5 us), and the tile's last part kSkFixCost to sum the other slots and write
+// fp16 (~11 us); one CTA per tile pays kTileEpiCost for its fp16 tile.  S minimises the
+// larger of the two kinds of CTA.  Returns the tiles and sets *split = S, or returns 0
+// when that saves less than a tenth.
+constexpr int64_t kSkSegCost = 8, kSkFixCost = 12, kTileEpiCost = 3;
+int64_t tc_streamk_plan(int64_t M, int64_t N, int64_t K, int num_sms, int* split) {
+  const int64_t bm = M > 128 ? 256 : 128;
+  const int64_t tiles = ((M + bm - 1) / bm) * ((N + BN - 1) / BN);
+  const int64_t kt = K / BK;
+  if (tiles <= 0 || 2 * tiles < num_sms || tiles >= num_sms || tiles > kMaxCounters) return 0;
+  const int64_t g2 = num_sms - tiles;
+  int64_t best = -1, best_s = 0;
+  for (int64_t s = (kt + 1) / 2; s < kt; ++s) {
+    const int64_t L = kt - s;
+    const int64_t lo = tiles * L / g2, hi = (tiles * L + g2 - 1) / g2;   // share lengths
+    if (lo < L) continue;                       // a tail would reach three sharers
+    const int64_t segs = (hi + L - 2) / L + 1;  // tiles a share of hi steps can reach
+    if (segs > kMaxSeg) continue;
+    const int64_t cost = std::max(s, hi + kSkSegCost * (segs - 1)) + kSkFixCost;
+    if (best < 0 || cost < best) {
+      best = cost;
+      best_s = s;
+    }
+  }
+  if (best < 0 || 10 * best > 9 * (kt + kTileEpiCost)) return 0;
+  if (split) *split = (int)best_s;
+  return tiles;
+}
+
 size_t tc_workspace_bytes(int64_t M, int64_t N, int64_t K, int num_sms) {
   const int s = tc_splits(M, N, K, num_sms);
-  return s > 1 ? kCounterRegionBytes + (size_t)s * M * N * sizeof(float) : 0;
+  if (s > 1) return kCounterRegionBytes + (size_t)s * M * N * sizeof(float);
+  const int64_t sk = tc_streamk_plan(M, N, K, num_sms, nullptr);
+  if (sk > 0) {
+    const int64_t bm = M > 128 ? 256 : 128;
+    return kCounterRegionBytes + (size_t)sk * kSkSlots * bm * BN * sizeof(float);
+  }
+  return 0;
 }
 
 bool tc_supported(const void* x, int64_t ldx, const int32_t* qweight, const int32_t* qzeros,
@@ -714,17 +999,35 @@ cudaError_t launch_gemm_tc(const void* x, int64_t ldx, const int32_t* qweight,
   a.M = M; a.N = N; a.K = K; a.gs = group_size;
   a.status = dev_status;
   a.bias = static_cast<const __half*>(bias);
-  // split-K when the caller's workspace holds the partials (after the decode kernels'
-  // counter region, which must stay zero); otherwise one CTA per tile
+  // split-K or stream-K when the caller's workspace holds the partials (after the decode
+  // kernels' counter region, which must stay zero); otherwise one CTA per tile
   a.splits = tc_splits(M, N, K, num_sms);
   a.part = nullptr;
+  a.streamk = 0;
+  a.tiles_n = (N + BN - 1) / BN;
+  a.sk_tiles = 0;
+  a.sk_split = 0;
+  a.sk_part = nullptr;
+  a.sk_cnt = nullptr;
+  const bool ws_ok = workspace && al16(workspace) &&
+                     workspace_bytes >= tc_workspace_bytes(M, N, K, num_sms);
   if (a.splits > 1) {
-    if (workspace && al16(workspace) && workspace_bytes >= tc_workspace_bytes(M, N, K, num_sms))
+    if (ws_ok)
       a.part = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterRegionBytes);
     else
       a.splits = 1;
   }
   dim3 grid((M + BM - 1) / BM, (N + BN - 1) / BN, a.splits);
+  int sk_split = 0;
+  const int64_t sk_tiles = a.splits == 1 ? tc_streamk_plan(M, N, K, num_sms, &sk_split) : 0;
+  if (sk_tiles > 0 && ws_ok) {
+    a.streamk = 1;
+    a.sk_tiles = (int)sk_tiles;
+    a.sk_split = sk_split;
+    a.sk_cnt = static_cast<int*>(workspace);
+    a.sk_part = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterRegionBytes);
+    grid = dim3(num_sms, 1, 1);
+  }
   if (nacc == 2)
     gemm_tc_kernel<2><<<grid, kThreads, Geo<2>::SMEM_BYTES, stream>>>(tmA, tmW, tmS, tmZ, a);
   else

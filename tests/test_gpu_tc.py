@@ -143,3 +143,51 @@ def test_tc_split_k(cuda, M, K, N):
     torch.cuda.synchronize()
     assert O.max_rel_err(out.float().cpu().numpy(), full.cpu().numpy()) <= TOL
     assert awq_b200.device_status() == 0
+
+
+@pytest.mark.parametrize("M,K,N", [
+    (2048, 18944, 3584),    # down: 8 x 14 = 112 tiles on 148 SMs, shares reach 4 tiles
+    (1536, 18944, 3584),    # 6 x 14 = 84 tiles
+    (1536, 3584, 3584),     # 84 tiles, 56 K steps: short tails
+    (1536, 18944, 4608),    # 6 x 18 = 108 tiles
+    (2000, 18944, 3360),    # ragged last row tile and last column tile
+])
+def test_tc_stream_k(cuda, M, K, N):
+    """Output tiles that fill between half and most of one wave (stream-K): one CTA per
+    tile runs the tile's first K steps, the other SMs' CTAs share the tiles' last steps;
+    each tile, in two or three parts, is summed from fp32 slots by the last CTA to finish
+    a part, in slot order.  Checked against an fp32
+    product of the exactly dequantized weights and the CPU oracle on three 64-column
+    blocks; repeated calls give the same bits (counters reset, fixed summation order); the
+    bias is added once; without a workspace the kernel runs one CTA per tile."""
+    import ctypes
+    import awq_b200
+    import awq_b200._lib as L
+    qw, qz, s = O.make_awq_layer(K, N, 128, seed=M + K)
+    x = O.make_x(M, K, seed=M)
+    dx, dqw, dqz, ds = _dev(cuda, x, qw, qz, s)
+    lib = L.load()
+    assert lib.awq_gemm_workspace_bytes(M, N, K, 128) > 0      # the stream-K slots
+    a = awq_b200.gemm(dx, dqw, dqz, ds, 128, path=awq_b200.AWQ_PATH_TC)
+    b = awq_b200.gemm(dx, dqw, dqz, ds, 128, path=awq_b200.AWQ_PATH_TC)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+    full = dx.float() @ awq_b200.dequant(dqw, dqz, ds, 128).float()
+    assert O.max_rel_err(a.float().cpu().numpy(), full.cpu().numpy()) <= TOL
+    rows = slice(0, min(M, 64))
+    for c0 in (0, (N // 2) // 64 * 64, N - 64):
+        ref = O.awq_gemm_f32(x[rows], qw[:, c0 // 8:(c0 + 64) // 8], qz[:, c0 // 8:(c0 + 64) // 8],
+                             s[:, c0:c0 + 64], 128)
+        assert O.max_rel_err(a[rows, c0:c0 + 64].float().cpu().numpy(), ref) <= TOL, c0
+    bias = torch.from_numpy(np.random.default_rng(5).uniform(-1, 1, N).astype(np.float16)).to(cuda)
+    ab = awq_b200.gemm(dx, dqw, dqz, ds, 128, bias=bias)
+    assert O.max_rel_err(ab.float().cpu().numpy(), (full + bias.float()).cpu().numpy()) <= TOL
+    out = torch.empty((M, N), dtype=torch.float16, device=cuda)
+    rc = lib.awq_gemm_f16_ex(dx.data_ptr(), K, dqw.data_ptr(), dqz.data_ptr(), ds.data_ptr(),
+                             out.data_ptr(), N, M, N, K, 128, None, 0,
+                             ctypes.c_void_p(torch.cuda.current_stream().cuda_stream),
+                             awq_b200.AWQ_PATH_TC)
+    assert rc == 0, lib.awq_last_error()
+    torch.cuda.synchronize()
+    assert O.max_rel_err(out.float().cpu().numpy(), full.cpu().numpy()) <= TOL
+    assert awq_b200.device_status() == 0
