@@ -6,18 +6,22 @@
 // 64x64 tiles on mma.sync) for M > 8.  The prefill kernel's CTA computes a 128 x 256 tile of
 // out = x @ W with fp32 accumulation in tensor memory:
 //
-//   warp 0      TMA producer: per 64-deep K step loads the x tile (128 x 64 fp16,
-//               128-byte swizzle), the packed weight tile (64 rows x 32 words), one
-//               row of scales (256 fp16) and one row of packed zeros (32 words)
-//               into a 4-stage ring, completion on tfull[s]
+//   warp 0      TMA producer: per 64-deep K step loads the packed weight tile (64 rows
+//               x 32 words), one row of scales (256 fp16) and one row of packed zeros
+//               (32 words) into the weight ring (rfull[s]), and the x tile (128 or 256
+//               x 64 fp16, 128-byte swizzle) into the x ring (afull[s]).  An x tile is
+//               held until its MMAs complete, a weight tile only until it has been
+//               dequantized, so the x ring is the deeper one: its depth x the K step
+//               time must cover the load latency under load (~1.5 us) plus the
+//               dequant and the MMAs
 //   warps 2..9  dequant: int4 -> fp16 W tile, bit-exact (fp16 (w - z) * scale), one
-//               8-row k-group per warp, written into a separate 3-stage ring as the
-//               UMMA B operand in the MN-major 128-byte-swizzled canonical layout,
-//               then fence.proxy.async + arrive on bfull[s]; after the K loop the
-//               same warps run the epilogue
+//               8-row k-group per warp, written into the B ring as the UMMA B operand
+//               in the MN-major 128-byte-swizzled canonical layout, then
+//               fence.proxy.async + arrive on bfull[s] and rempty[s]; after the K loop
+//               the same warps run the epilogue
 //   warp 1      TMEM allocation (256 columns) and the single-thread MMA issue:
 //               4 x tcgen05.mma.kind::f16 (M=128, N=256, K=16) per K step, then
-//               tcgen05.commit -> tempty / bempty free both rings' stages; the last
+//               tcgen05.commit -> aempty / bempty free the x and B stages; the last
 //               commit signals the accumulator to the epilogue
 //   epilogue    tcgen05.ld 32x32b (a warp reads its TMEM lane quarter = 32 rows, the
 //               two warps of a quarter split the 256 columns), fp32 -> fp16, 16-byte
@@ -60,20 +64,23 @@ constexpr uint32_t kIdesc = sm100::idesc_f16_f32(128, BN, /*a_mn*/ 0, /*b_mn*/ 1
 template <int NACC>
 struct Geo {
   static constexpr int BM = 128 * NACC;
-  static constexpr int TSTAGES = NACC == 1 ? 4 : 3;   // TMA ring depth
+  static constexpr int ASTAGES = NACC == 1 ? 5 : 4;   // x ring depth
+  static constexpr int RSTAGES = NACC == 1 ? 4 : 3;   // packed weight / scale / zero ring
   static constexpr int BSTAGES = NACC == 1 ? 3 : 2;   // dequantized B ring depth
-  static constexpr uint32_t A_BYTES = BM * BK * 2;
-  static constexpr uint32_t TX_BYTES = A_BYTES + RAW_BYTES + SC_BYTES + ZR_BYTES;
-  static constexpr uint32_t T_RAW = A_BYTES, T_SC = T_RAW + RAW_BYTES, T_ZR = T_SC + SC_BYTES;
-  static constexpr uint32_t T_STAGE = (T_ZR + ZR_BYTES + 1023) / 1024 * 1024;
-  static constexpr uint32_t OFF_T = 0;
-  static constexpr uint32_t OFF_B = OFF_T + TSTAGES * T_STAGE;
-  // tfull, tempty, bfull, bempty, accf, tmem empty, drain
+  static constexpr uint32_t A_BYTES = BM * BK * 2;    // 1 KB multiple (swizzle atoms)
+  static constexpr uint32_t R_RAW = 0, R_SC = RAW_BYTES, R_ZR = R_SC + SC_BYTES;
+  static constexpr uint32_t R_TX = RAW_BYTES + SC_BYTES + ZR_BYTES;
+  static constexpr uint32_t R_STAGE = (R_TX + 127) / 128 * 128;
+  static constexpr uint32_t OFF_A = 0;
+  static constexpr uint32_t OFF_R = OFF_A + ASTAGES * A_BYTES;
+  static constexpr uint32_t OFF_B = (OFF_R + RSTAGES * R_STAGE + 1023) / 1024 * 1024;
+  // afull, aempty, rfull, rempty, bfull, bempty, accf, tmem empty, drain
   static constexpr uint32_t OFF_BAR = OFF_B + BSTAGES * B_BYTES;
-  static constexpr uint32_t NBARS = 2 * TSTAGES + 2 * BSTAGES + 3;
+  static constexpr uint32_t NBARS = 2 * ASTAGES + 2 * RSTAGES + 2 * BSTAGES + 3;
   static constexpr uint32_t OFF_MISC = OFF_BAR + NBARS * 8;
   static constexpr uint32_t SMEM_BYTES = OFF_MISC + 16 + 1024;      // + alignment slack
   static constexpr uint32_t TMEM_COLS = 256 * NACC;
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
 };
 
 struct TcArgs {
@@ -153,10 +160,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmZ,
                const TcArgs args) {
   using G = Geo<NACC>;
-  constexpr int BM = G::BM, TSTAGES = G::TSTAGES, BSTAGES = G::BSTAGES;
-  constexpr uint32_t T_STAGE = G::T_STAGE, T_RAW = G::T_RAW, T_SC = G::T_SC, T_ZR = G::T_ZR;
-  constexpr uint32_t OFF_T = G::OFF_T, OFF_B = G::OFF_B, OFF_BAR = G::OFF_BAR, OFF_MISC = G::OFF_MISC;
-  constexpr uint32_t TX_BYTES = G::TX_BYTES, TMEM_COLS = G::TMEM_COLS;
+  constexpr int BM = G::BM, ASTAGES = G::ASTAGES, RSTAGES = G::RSTAGES, BSTAGES = G::BSTAGES;
+  constexpr uint32_t A_BYTES = G::A_BYTES, R_STAGE = G::R_STAGE, R_RAW = G::R_RAW, R_SC = G::R_SC,
+                     R_ZR = G::R_ZR, R_TX = G::R_TX;
+  constexpr uint32_t OFF_A = G::OFF_A, OFF_R = G::OFF_R, OFF_B = G::OFF_B, OFF_BAR = G::OFF_BAR,
+                     OFF_MISC = G::OFF_MISC;
+  constexpr uint32_t TMEM_COLS = G::TMEM_COLS;
   extern __shared__ unsigned char smem_raw[];
   const uint32_t base_raw = sm100::smem_u32(smem_raw);
   const uint32_t sbase = (base_raw + 1023u) & ~1023u;        // 1 KB aligned (swizzle atoms)
@@ -215,11 +224,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       }
   }
 
-  auto bar_tfull = [&](int s) { return sbase + OFF_BAR + 8u * s; };
-  auto bar_tempty = [&](int s) { return sbase + OFF_BAR + 8u * (TSTAGES + s); };
-  auto bar_bfull = [&](int s) { return sbase + OFF_BAR + 8u * (2 * TSTAGES + s); };
-  auto bar_bempty = [&](int s) { return sbase + OFF_BAR + 8u * (2 * TSTAGES + BSTAGES + s); };
-  const uint32_t bar_accf = sbase + OFF_BAR + 8u * (2 * TSTAGES + 2 * BSTAGES);
+  auto bar_afull = [&](int s) { return sbase + OFF_BAR + 8u * s; };
+  auto bar_aempty = [&](int s) { return sbase + OFF_BAR + 8u * (ASTAGES + s); };
+  auto bar_rfull = [&](int s) { return sbase + OFF_BAR + 8u * (2 * ASTAGES + s); };
+  auto bar_rempty = [&](int s) { return sbase + OFF_BAR + 8u * (2 * ASTAGES + RSTAGES + s); };
+  auto bar_bfull = [&](int s) { return sbase + OFF_BAR + 8u * (2 * ASTAGES + 2 * RSTAGES + s); };
+  auto bar_bempty = [&](int s) {
+    return sbase + OFF_BAR + 8u * (2 * ASTAGES + 2 * RSTAGES + BSTAGES + s);
+  };
+  const uint32_t bar_accf = sbase + OFF_BAR + 8u * (2 * ASTAGES + 2 * RSTAGES + 2 * BSTAGES);
   const uint32_t bar_tmem_empty = bar_accf + 8u;   // epilogue read the accumulator (stream-K)
   const uint32_t bar_drain = bar_accf + 16u;       // every MMA of this CTA completed
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(sgen + OFF_MISC);
@@ -227,9 +240,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   volatile int* last_flag = reinterpret_cast<volatile int*>(sgen + OFF_MISC + 8);
 
   if (tid == 0) {
-    for (int s = 0; s < TSTAGES; ++s) {
-      sm100::mbar_init(bar_tfull(s), 1);
-      sm100::mbar_init(bar_tempty(s), 1);
+    for (int s = 0; s < ASTAGES; ++s) {
+      sm100::mbar_init(bar_afull(s), 1);
+      sm100::mbar_init(bar_aempty(s), 1);
+    }
+    for (int s = 0; s < RSTAGES; ++s) {
+      sm100::mbar_init(bar_rfull(s), 1);
+      sm100::mbar_init(bar_rempty(s), kDeqWarps);  // one arrive per dequant warp
     }
     for (int s = 0; s < BSTAGES; ++s) {
       sm100::mbar_init(bar_bfull(s), kDeqWarps);   // one arrive per dequant warp
@@ -257,30 +274,43 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   if (warp == 0) {
     // ------------------------------------------------------------- TMA producer ----
     if (lane == 0) {
-      int j = 0;                                 // the CTA's step counter (ring position)
+      // the CTA's step counter j is both rings' position; nr / na count the weight and
+      // x stages issued (they differ by one when an abort falls between the two)
+      int j = 0, nr = 0, na = 0;
       for (int si = 0; si < nseg && !*abort_flag; ++si) {
         const TcSeg& sg = seg[si];
         for (int kt = sg.k0; kt < sg.k1; ++kt, ++j) {
-          const int s = j % TSTAGES;
-          if (j >= TSTAGES &&
-              !sm100::mbar_wait_bounded(bar_tempty(s), ((j / TSTAGES) & 1) ^ 1, args.status)) {
+          const int rs = j % RSTAGES, as = j % ASTAGES;
+          const int k0 = kt * BK;
+          const int grp = k0 / args.gs;
+          if (j >= RSTAGES &&
+              !sm100::mbar_wait_bounded(bar_rempty(rs), ((j / RSTAGES) & 1) ^ 1, args.status)) {
             *abort_flag = 1;
             break;
           }
           if (*abort_flag) break;
-          const int k0 = kt * BK;
-          const int grp = k0 / args.gs;
-          const uint32_t st = sbase + OFF_T + s * T_STAGE;
-          sm100::mbar_arrive_expect_tx(bar_tfull(s), TX_BYTES);
-          sm100::tma_load_2d(st, &tmA, bar_tfull(s), k0, sg.tile_m * BM);
-          sm100::tma_load_2d(st + T_RAW, &tmW, bar_tfull(s), sg.tile_n * (BN / 8), k0);
-          sm100::tma_load_2d(st + T_SC, &tmS, bar_tfull(s), sg.tile_n * BN, grp);
-          sm100::tma_load_2d(st + T_ZR, &tmZ, bar_tfull(s), sg.tile_n * (BN / 8), grp);
+          const uint32_t rst = sbase + OFF_R + rs * R_STAGE;
+          sm100::mbar_arrive_expect_tx(bar_rfull(rs), R_TX);
+          sm100::tma_load_2d(rst + R_RAW, &tmW, bar_rfull(rs), sg.tile_n * (BN / 8), k0);
+          sm100::tma_load_2d(rst + R_SC, &tmS, bar_rfull(rs), sg.tile_n * BN, grp);
+          sm100::tma_load_2d(rst + R_ZR, &tmZ, bar_rfull(rs), sg.tile_n * (BN / 8), grp);
+          ++nr;
+          if (j >= ASTAGES &&
+              !sm100::mbar_wait_bounded(bar_aempty(as), ((j / ASTAGES) & 1) ^ 1, args.status)) {
+            *abort_flag = 1;
+            break;
+          }
+          if (*abort_flag) break;
+          sm100::mbar_arrive_expect_tx(bar_afull(as), A_BYTES);
+          sm100::tma_load_2d(sbase + OFF_A + as * A_BYTES, &tmA, bar_afull(as), k0, sg.tile_m * BM);
+          ++na;
         }
       }
-      // drain: the copies of the last (up to) TSTAGES steps must land before exit
-      for (int i = (j > TSTAGES ? j - TSTAGES : 0); i < j; ++i)
-        sm100::mbar_wait_bounded(bar_tfull(i % TSTAGES), (i / TSTAGES) & 1, args.status);
+      // drain: the last (up to) RSTAGES weight and ASTAGES x copies must land before exit
+      for (int i = (nr > RSTAGES ? nr - RSTAGES : 0); i < nr; ++i)
+        sm100::mbar_wait_bounded(bar_rfull(i % RSTAGES), (i / RSTAGES) & 1, args.status);
+      for (int i = (na > ASTAGES ? na - ASTAGES : 0); i < na; ++i)
+        sm100::mbar_wait_bounded(bar_afull(i % ASTAGES), (i / ASTAGES) & 1, args.status);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -295,14 +325,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           sm100::tc_fence_after();
         }
         for (int kt = sg.k0; kt < sg.k1 && !*abort_flag; ++kt, ++j) {
-          const int ts = j % TSTAGES, bs = j % BSTAGES;
-          if (!sm100::mbar_wait_bounded(bar_bfull(bs), (j / BSTAGES) & 1, args.status)) {
+          const int as = j % ASTAGES, bs = j % BSTAGES;
+          if (!sm100::mbar_wait_bounded(bar_bfull(bs), (j / BSTAGES) & 1, args.status) ||
+              !sm100::mbar_wait_bounded(bar_afull(as), (j / ASTAGES) & 1, args.status)) {
             *abort_flag = 1;
             break;
           }
           if (*abort_flag) break;
           sm100::tc_fence_after();
-          const uint32_t a0 = sbase + OFF_T + ts * T_STAGE;
+          const uint32_t a0 = sbase + OFF_A + as * A_BYTES;
           const uint32_t b0 = sbase + OFF_B + bs * B_BYTES;
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
@@ -313,7 +344,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
               sm100::umma_f16(tmem_d + 256 * h, ad, bd, kIdesc, (kt != sg.k0 || kk != 0) ? 1u : 0u);
             }
           }
-          sm100::umma_commit(bar_tempty(ts));    // x tile and packed inputs consumed
+          sm100::umma_commit(bar_aempty(as));    // x tile consumed
           sm100::umma_commit(bar_bempty(bs));    // dequantized B consumed
         }
         sm100::umma_commit(bar_accf);            // phase si: the segment's MMAs have completed
@@ -329,8 +360,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     for (int si = 0; si < nseg; ++si) {
       const TcSeg& sg = seg[si];
       for (int kt = sg.k0; kt < sg.k1 && !*abort_flag; ++kt, ++j) {
-        const int ts = j % TSTAGES, bs = j % BSTAGES;
-        if (!sm100::mbar_wait_bounded(bar_tfull(ts), (j / TSTAGES) & 1, args.status)) {
+        const int rs = j % RSTAGES, bs = j % BSTAGES;
+        if (!sm100::mbar_wait_bounded(bar_rfull(rs), (j / RSTAGES) & 1, args.status)) {
           *abort_flag = 1;
           break;
         }
@@ -340,10 +371,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           break;
         }
         if (*abort_flag) break;
-        const unsigned char* tst = sgen + OFF_T + ts * T_STAGE;
-        const uint32_t* raw = reinterpret_cast<const uint32_t*>(tst + T_RAW) + dw * 8 * (BN / 8);
-        const uint32_t zw = reinterpret_cast<const uint32_t*>(tst + T_ZR)[w];
-        const uint4 s4 = reinterpret_cast<const uint4*>(tst + T_SC)[w];
+        const unsigned char* rst = sgen + OFF_R + rs * R_STAGE;
+        const uint32_t* raw = reinterpret_cast<const uint32_t*>(rst + R_RAW) + dw * 8 * (BN / 8);
+        const uint32_t zw = reinterpret_cast<const uint32_t*>(rst + R_ZR)[w];
+        const uint4 s4 = reinterpret_cast<const uint4*>(rst + R_SC)[w];
         uint32_t zc[4], sc[4] = {s4.x, s4.y, s4.z, s4.w};
         zero_consts(zw, zc);
         uint32_t wv[8];
@@ -359,7 +390,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
         sm100::fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) sm100::mbar_arrive(bar_bfull(bs));
+        if (lane == 0) {
+          sm100::mbar_arrive(bar_bfull(bs));
+          sm100::mbar_arrive(bar_rempty(rs));   // the warp's reads of the weight stage are done
+        }
       }
 
       // ----------------------------------------------------------- epilogue --------
