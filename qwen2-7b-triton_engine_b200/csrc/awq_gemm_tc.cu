@@ -103,6 +103,13 @@ struct TcArgs {
   int sk_split;
   float* sk_part;       // [tiles][kSkSlots][BM * 256] fp32, each slot in fragment order
   int* sk_cnt;          // per-tile arrivals, zero between calls
+  // persistent (streamk == 0, splits == 1; more tiles than CTAs): CTA c works on tiles
+  // c, c + gridDim.x, ... of the tiles_m x tiles_n tiles (tile t = (t % tiles_m,
+  // t / tiles_m), the order of the tile grid's blocks), one after another; the producer
+  // loads the next tile's first stages while the epilogue writes the current one
+  int persistent;
+  int tiles_m;
+  int tiles_total;
 };
 
 constexpr int kSkSlots = 3;   // CTAs per tile under stream-K, at most (the tail's sharers <= 2)
@@ -173,18 +180,20 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
-  const int tile_m = blockIdx.x, tile_n = blockIdx.y;
   // this CTA's work as segments (tile, K steps).  Tile grid: the tile of (blockIdx.x,
   // blockIdx.y), K steps split over blockIdx.z (the ranges of one tile differ by at most
   // one step).  Stream-K: CTA c < tiles takes steps [0, S) of tile c (slot 0); CTA
   // tiles + j of the G2 = gridDim.x - tiles others takes linear steps
   // [j TT / G2, (j + 1) TT / G2) of the tails, TT = tiles x L with L = K/64 - S, step u
   // being step S + u % L of tile u / L (slots 1 and 2 of a tile: its tail's first and
-  // second sharer).  The rings below count the CTA's steps from 0 across its segments.
+  // second sharer).  Persistent: tile blockIdx.x + i gridDim.x for segment i (seg_at).
+  // The rings below count the CTA's steps from 0 across its segments.
   const int kt_all = args.K / BK;
   TcSeg seg[kMaxSeg];
   int nseg = 0;
-  if (!args.streamk) {
+  if (args.persistent) {
+    nseg = (args.tiles_total - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+  } else if (!args.streamk) {
     const int kt0 = (int)((int64_t)blockIdx.z * kt_all / args.splits);
     const int kt1 = (int)((int64_t)(blockIdx.z + 1) * kt_all / args.splits);
     seg[0] = TcSeg{(int)blockIdx.x, (int)blockIdx.y, kt0, kt1, (int)blockIdx.z, args.splits};
@@ -224,6 +233,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       }
   }
 
+  auto seg_at = [&](int si) -> TcSeg {
+    if (args.persistent) {
+      const int t = (int)blockIdx.x + si * (int)gridDim.x;
+      return TcSeg{t % args.tiles_m, t / args.tiles_m, 0, kt_all, 0, 1};
+    }
+    return seg[si];
+  };
   auto bar_afull = [&](int s) { return sbase + OFF_BAR + 8u * s; };
   auto bar_aempty = [&](int s) { return sbase + OFF_BAR + 8u * (ASTAGES + s); };
   auto bar_rfull = [&](int s) { return sbase + OFF_BAR + 8u * (2 * ASTAGES + s); };
@@ -278,7 +294,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       // x stages issued (they differ by one when an abort falls between the two)
       int j = 0, nr = 0, na = 0;
       for (int si = 0; si < nseg && !*abort_flag; ++si) {
-        const TcSeg& sg = seg[si];
+        const TcSeg sg = seg_at(si);
         for (int kt = sg.k0; kt < sg.k1; ++kt, ++j) {
           const int rs = j % RSTAGES, as = j % ASTAGES;
           const int k0 = kt * BK;
@@ -318,7 +334,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     if (lane == 0) {
       int j = 0;
       for (int si = 0; si < nseg; ++si) {
-        const TcSeg& sg = seg[si];
+        const TcSeg sg = seg_at(si);
         // a second segment reuses the accumulator: wait until the epilogue has read it
         if (si > 0) {
           if (!sm100::mbar_wait_bounded(bar_tmem_empty, (si - 1) & 1, args.status)) *abort_flag = 1;
@@ -358,7 +374,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const uint32_t bst_lane = (uint32_t)(w >> 3) * B_LBO + (uint32_t)dw * B_SBO;
     int j = 0;
     for (int si = 0; si < nseg; ++si) {
-      const TcSeg& sg = seg[si];
+      const TcSeg sg = seg_at(si);
       for (int kt = sg.k0; kt < sg.k1 && !*abort_flag; ++kt, ++j) {
         const int rs = j % RSTAGES, bs = j % BSTAGES;
         if (!sm100::mbar_wait_bounded(bar_rfull(rs), (j / RSTAGES) & 1, args.status)) {
@@ -1041,6 +1057,9 @@ cudaError_t launch_gemm_tc(const void* x, int64_t ldx, const int32_t* qweight,
   a.tiles_n = (N + BN - 1) / BN;
   a.sk_tiles = 0;
   a.sk_split = 0;
+  a.persistent = 0;
+  a.tiles_m = (M + BM - 1) / BM;
+  a.tiles_total = a.tiles_m * a.tiles_n;
   a.sk_part = nullptr;
   a.sk_cnt = nullptr;
   const bool ws_ok = workspace && al16(workspace) &&
@@ -1060,6 +1079,9 @@ cudaError_t launch_gemm_tc(const void* x, int64_t ldx, const int32_t* qweight,
     a.sk_split = sk_split;
     a.sk_cnt = static_cast<int*>(workspace);
     a.sk_part = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterRegionBytes);
+    grid = dim3(num_sms, 1, 1);
+  } else if (a.splits == 1 && a.tiles_total > num_sms) {
+    a.persistent = 1;                    // one CTA per SM, tiles taken in grid order
     grid = dim3(num_sms, 1, 1);
   }
   if (nacc == 2)

@@ -191,3 +191,37 @@ def test_tc_stream_k(cuda, M, K, N):
     torch.cuda.synchronize()
     assert O.max_rel_err(out.float().cpu().numpy(), full.cpu().numpy()) <= TOL
     assert awq_b200.device_status() == 0
+
+
+@pytest.mark.parametrize("M,K,N", [
+    (1000, 1024, 10016),    # 4 x 40 = 160 tiles of 256 x 256, ragged last row and column tile
+    (300, 2048, 37888),     # 2 x 148 = 296 tiles: every CTA takes two
+    (100, 512, 40000),      # 128-row tiles: 1 x 157
+])
+def test_tc_persistent(cuda, M, K, N):
+    """More output tiles than SMs: one CTA per SM takes tiles c, c + SMs, ... in turn, the
+    next tile's loads overlapping the current tile's epilogue.  Checked against an fp32
+    product of the exactly dequantized weights, the CPU oracle on 64-column blocks at both
+    ends, with the bias, and bit-equal on a repeated call."""
+    import awq_b200
+    qw, qz, s = O.make_awq_layer(K, N, 128, seed=M + 7)
+    x = O.make_x(M, K, seed=K + 3)
+    dx, dqw, dqz, ds = _dev(cuda, x, qw, qz, s)
+    sms = torch.cuda.get_device_properties(cuda).multi_processor_count
+    bm = 256 if M > 128 else 128
+    assert ((M + bm - 1) // bm) * ((N + 255) // 256) > sms
+    a = awq_b200.gemm(dx, dqw, dqz, ds, 128, path=awq_b200.AWQ_PATH_TC)
+    b = awq_b200.gemm(dx, dqw, dqz, ds, 128, path=awq_b200.AWQ_PATH_TC)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+    full = dx.float() @ awq_b200.dequant(dqw, dqz, ds, 128).float()
+    assert O.max_rel_err(a.float().cpu().numpy(), full.cpu().numpy()) <= TOL
+    rows = slice(M - min(M, 64), M)
+    for c0 in (0, N - 64):
+        ref = O.awq_gemm_f32(x[rows], qw[:, c0 // 8:(c0 + 64) // 8], qz[:, c0 // 8:(c0 + 64) // 8],
+                             s[:, c0:c0 + 64], 128)
+        assert O.max_rel_err(a[rows, c0:c0 + 64].float().cpu().numpy(), ref) <= TOL, c0
+    bias = torch.from_numpy(np.random.default_rng(9).uniform(-1, 1, N).astype(np.float16)).to(cuda)
+    ab = awq_b200.gemm(dx, dqw, dqz, ds, 128, bias=bias)
+    assert O.max_rel_err(ab.float().cpu().numpy(), (full + bias.float()).cpu().numpy()) <= TOL
+    assert awq_b200.device_status() == 0
