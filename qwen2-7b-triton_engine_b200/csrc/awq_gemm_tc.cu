@@ -375,41 +375,45 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     int j = 0;
     for (int si = 0; si < nseg; ++si) {
       const TcSeg sg = seg_at(si);
-      for (int kt = sg.k0; kt < sg.k1 && !*abort_flag; ++kt, ++j) {
+      for (int kt = sg.k0; kt < sg.k1; ++kt, ++j) {
         const int rs = j % RSTAGES, bs = j % BSTAGES;
+        // The packed tile is dequantized into registers as soon as it lands and its weight
+        // stage is released at once; only the shared-memory stores wait for the B stage
+        // (freed by the MMAs of BSTAGES steps ago), so the dequant runs under the MMAs in
+        // flight instead of between them.
         if (!sm100::mbar_wait_bounded(bar_rfull(rs), (j / RSTAGES) & 1, args.status)) {
           *abort_flag = 1;
           break;
         }
+        if (*abort_flag) break;
+        const uint32_t rst = sbase + OFF_R + rs * R_STAGE;
+        const uint32_t zw = sm100::ld_shared_u32(rst + R_ZR + 4u * (uint32_t)w);
+        const uint4 s4 = sm100::ld_shared_v4(rst + R_SC + 16u * (uint32_t)w);
+        uint32_t wv[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          wv[i] = sm100::ld_shared_u32(rst + R_RAW + 4u * (uint32_t)((dw * 8 + i) * (BN / 8) + w));
+        uint32_t zc[4], sc[4] = {s4.x, s4.y, s4.z, s4.w};
+        zero_consts(zw, zc);
+        uint32_t d[8][4];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dequant_word(wv[i], zc, sc, d[i]);
+        __syncwarp();
+        if (lane == 0) sm100::mbar_arrive(bar_rempty(rs));   // the warp's reads are done
         if (j >= BSTAGES &&
             !sm100::mbar_wait_bounded(bar_bempty(bs), ((j / BSTAGES) & 1) ^ 1, args.status)) {
           *abort_flag = 1;
           break;
         }
-        if (*abort_flag) break;
-        const unsigned char* rst = sgen + OFF_R + rs * R_STAGE;
-        const uint32_t* raw = reinterpret_cast<const uint32_t*>(rst + R_RAW) + dw * 8 * (BN / 8);
-        const uint32_t zw = reinterpret_cast<const uint32_t*>(rst + R_ZR)[w];
-        const uint4 s4 = reinterpret_cast<const uint4*>(rst + R_SC)[w];
-        uint32_t zc[4], sc[4] = {s4.x, s4.y, s4.z, s4.w};
-        zero_consts(zw, zc);
-        uint32_t wv[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) wv[i] = raw[i * (BN / 8) + w];
         const uint32_t bstage = sbase + OFF_B + bs * B_BYTES + bst_lane;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          uint32_t d[4];
-          dequant_word(wv[i], zc, sc, d);
           const uint32_t addr = bstage + (uint32_t)i * 128u + ((uint32_t)((w & 7) ^ i) << 4);
-          sm100::st_shared_v4(addr, d[0], d[1], d[2], d[3]);
+          sm100::st_shared_v4(addr, d[i][0], d[i][1], d[i][2], d[i][3]);
         }
         sm100::fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) {
-          sm100::mbar_arrive(bar_bfull(bs));
-          sm100::mbar_arrive(bar_rempty(rs));   // the warp's reads of the weight stage are done
-        }
+        if (lane == 0) sm100::mbar_arrive(bar_bfull(bs));
       }
 
       // ----------------------------------------------------------- epilogue --------
