@@ -354,6 +354,24 @@ int awq_gemm_f16_silu_mul(const void* x, int64_t ldx, const int32_t* qweight,
     if (e != cudaSuccess) return fail_cuda(e, "decode (TMA) kernel launch, SiLU-mul epilogue");
     return AWQ_OK;
   }
+  // Above 16 tokens, when the product would run on the tcgen05 kernel unsplit (its tiles
+  // fill at least half the SMs: every Qwen2-7B gate+up call), that kernel's epilogue does
+  // the SiLU-mul: a tile holds 128 gate and the matching 128 up columns, and only the
+  // [M, N/2] result is written.
+  if (M > 16 && N % 512 == 0 && aligned16(out) && ldo % 8 == 0 &&
+      awq::tc_supported(x, ldx, qweight, qzeros, scales, M, N, K, group_size)) {
+    const int64_t bm = M > 128 ? 256 : 128;
+    const int64_t tiles = ((M + bm - 1) / bm) * (N / 256);
+    if (2 * tiles >= d->num_sms) {
+      const char* why = nullptr;
+      cudaError_t e = awq::launch_gemm_tc(x, ldx, qweight, qzeros, scales, out, ldo, (int)M,
+                                          (int)N, (int)K, (int)group_size, d->num_sms, d->status,
+                                          st, &why, nullptr, nullptr, 0, /*silu=*/true);
+      if (why) return fail(AWQ_ERR_UNSUPPORTED, "tcgen05 SiLU-mul path: %s", why);
+      if (e != cudaSuccess) return fail_cuda(e, "tcgen05 GEMM launch, SiLU-mul epilogue");
+      return AWQ_OK;
+    }
+  }
   const size_t off = silu_temp_offset(M, N, K, group_size);
   const size_t need = off + (size_t)M * N * 2;
   if (workspace_bytes < need)

@@ -68,9 +68,14 @@ struct Geo {
   static constexpr int RSTAGES = NACC == 1 ? 4 : 3;   // packed weight / scale / zero ring
   static constexpr int BSTAGES = NACC == 1 ? 3 : 2;   // dequantized B ring depth
   static constexpr uint32_t A_BYTES = BM * BK * 2;    // 1 KB multiple (swizzle atoms)
+  // every TMA destination starts on a 128-byte boundary: the SiLU-mul layout's second
+  // (up) zero box goes to R_ZR + 128, not right after the first 64-byte box
   static constexpr uint32_t R_RAW = 0, R_SC = RAW_BYTES, R_ZR = R_SC + SC_BYTES;
   static constexpr uint32_t R_TX = RAW_BYTES + SC_BYTES + ZR_BYTES;
-  static constexpr uint32_t R_STAGE = (R_TX + 127) / 128 * 128;
+  static constexpr uint32_t R_STAGE = (R_ZR + 2 * 128 + 127) / 128 * 128;
+  static_assert(R_SC % 128 == 0 && (R_SC + SC_BYTES / 2) % 128 == 0 && R_ZR % 128 == 0 &&
+                    (RAW_BYTES / 2) % 128 == 0 && R_STAGE % 128 == 0,
+                "TMA destinations 128-byte aligned");
   static constexpr uint32_t OFF_A = 0;
   static constexpr uint32_t OFF_R = OFF_A + ASTAGES * A_BYTES;
   static constexpr uint32_t OFF_B = (OFF_R + RSTAGES * R_STAGE + 1023) / 1024 * 1024;
@@ -110,7 +115,23 @@ struct TcArgs {
   int persistent;
   int tiles_m;
   int tiles_total;
+  // SiLU-mul epilogue (silu != 0; no split, no stream-K, no bias): columns [0, N/2) of the
+  // weights are the gate, [N/2, N) the up projection.  Tile n's 256 B-operand columns are
+  // gate columns [128 n, 128 n + 128) followed by the same up columns, loaded as two
+  // half-width boxes each, and the epilogue writes out[m, 128 n + c] =
+  // fp16(silu(g) * u) with g and u the fp16-rounded products (out is [M, N/2]).
+  int silu;
 };
+
+// silu(g) * u of fp32 products rounded to fp16 first, as the unfused sequence rounds its
+// product.  The sigmoid uses the hardware exponential and an approximate divide (two
+// MUFU operations), as the reference's Triton sigmoid does (kernels/silu_mul.py:35-36):
+// the epilogue runs while the tensor pipe waits for TMEM, and the IEEE forms cost ~10 us
+// per 256 x 256 tile there.
+__device__ __forceinline__ float silu_mul_rounded(float g, float u) {
+  const float x = __half2float(__float2half_rn(g)), y = __half2float(__float2half_rn(u));
+  return __fdividef(x, 1.0f + __expf(-x)) * y;
+}
 
 constexpr int kSkSlots = 3;   // CTAs per tile under stream-K, at most (the tail's sharers <= 2)
 constexpr int kMaxSeg = 8;    // tiles a CTA works on under stream-K, at most
@@ -307,9 +328,24 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           if (*abort_flag) break;
           const uint32_t rst = sbase + OFF_R + rs * R_STAGE;
           sm100::mbar_arrive_expect_tx(bar_rfull(rs), R_TX);
-          sm100::tma_load_2d(rst + R_RAW, &tmW, bar_rfull(rs), sg.tile_n * (BN / 8), k0);
-          sm100::tma_load_2d(rst + R_SC, &tmS, bar_rfull(rs), sg.tile_n * BN, grp);
-          sm100::tma_load_2d(rst + R_ZR, &tmZ, bar_rfull(rs), sg.tile_n * (BN / 8), grp);
+          if (!args.silu) {
+            sm100::tma_load_2d(rst + R_RAW, &tmW, bar_rfull(rs), sg.tile_n * (BN / 8), k0);
+            sm100::tma_load_2d(rst + R_SC, &tmS, bar_rfull(rs), sg.tile_n * BN, grp);
+            sm100::tma_load_2d(rst + R_ZR, &tmZ, bar_rfull(rs), sg.tile_n * (BN / 8), grp);
+          } else {
+            // gate half, then up half: [64 rows][16 words] twice, 128 + 128 scales, 16 + 16
+            // zero words (the maps' boxes are half as wide)
+            const int hw = args.N / 16, hn = args.N / 2;
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              sm100::tma_load_2d(rst + R_RAW + u * (RAW_BYTES / 2), &tmW, bar_rfull(rs),
+                                 u * hw + sg.tile_n * (BN / 16), k0);
+              sm100::tma_load_2d(rst + R_SC + u * (SC_BYTES / 2), &tmS, bar_rfull(rs),
+                                 u * hn + sg.tile_n * (BN / 2), grp);
+              sm100::tma_load_2d(rst + R_ZR + u * 128, &tmZ, bar_rfull(rs),
+                                 u * hw + sg.tile_n * (BN / 16), grp);
+            }
+          }
           ++nr;
           if (j >= ASTAGES &&
               !sm100::mbar_wait_bounded(bar_aempty(as), ((j / ASTAGES) & 1) ^ 1, args.status)) {
@@ -387,12 +423,19 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
         if (*abort_flag) break;
         const uint32_t rst = sbase + OFF_R + rs * R_STAGE;
-        const uint32_t zw = sm100::ld_shared_u32(rst + R_ZR + 4u * (uint32_t)w);
+        const uint32_t zw = sm100::ld_shared_u32(
+            rst + R_ZR + (args.silu ? (uint32_t)(w >> 4) * 128u + 4u * (uint32_t)(w & 15) : 4u * (uint32_t)w));
         const uint4 s4 = sm100::ld_shared_v4(rst + R_SC + 16u * (uint32_t)w);
         uint32_t wv[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-          wv[i] = sm100::ld_shared_u32(rst + R_RAW + 4u * (uint32_t)((dw * 8 + i) * (BN / 8) + w));
+        for (int i = 0; i < 8; ++i) {
+          // word w of row dw * 8 + i: one [64][32] block, or (SiLU-mul) the gate / up
+          // [64][16] blocks for w < 16 / w >= 16
+          const int r = dw * 8 + i;
+          const uint32_t off = args.silu ? (uint32_t)(w >> 4) * (RAW_BYTES / 2) + 4u * (uint32_t)(r * 16 + (w & 15))
+                                         : 4u * (uint32_t)(r * (BN / 8) + w);
+          wv[i] = sm100::ld_shared_u32(rst + R_RAW + off);
+        }
         uint32_t zc[4], sc[4] = {s4.x, s4.y, s4.z, s4.w};
         zero_consts(zw, zc);
         uint32_t d[8][4];
@@ -439,7 +482,28 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       const uint32_t stage = sbase + OFF_B + (uint32_t)dw * 2048u;
       const int row0 = sg.tile_m * BM + acc * 128 + q * 32;
       const bool live = ok && !*abort_flag;
-      if (!shared_tile) {
+      if (!shared_tile && args.silu) {
+        // gate chunk cg (TMEM columns 32 cg) with up chunk cg + 4 (columns 128 + 32 cg):
+        // NACC == 2: chunks 0..3 of this warp's accumulator; NACC == 1: the warp's half
+        const int g_lo = NACC == 2 ? 0 : half * 2, g_hi = NACC == 2 ? 4 : half * 2 + 2;
+        if (live) {
+#pragma unroll 1
+          for (int cg = g_lo; cg < g_hi; ++cg) {
+            uint32_t vg[32], vu[32];
+            sm100::tmem_ld_32x32b_x32(taddr + cg * 32, vg);
+            sm100::tmem_ld_32x32b_x32(taddr + 128 + cg * 32, vu);
+            sm100::tmem_ld_wait();
+            const int col = sg.tile_n * (BN / 2) + cg * 32;
+            uint32_t h[16];
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj)
+              h[jj] = h2_as_u32(__floats2half2_rn(
+                  silu_mul_rounded(__uint_as_float(vg[2 * jj]), __uint_as_float(vu[2 * jj])),
+                  silu_mul_rounded(__uint_as_float(vg[2 * jj + 1]), __uint_as_float(vu[2 * jj + 1]))));
+            store_rows_staged(stage, h, args.out, args.ldo, row0, col, args.M, lane);
+          }
+        }
+      } else if (!shared_tile) {
         if (live) {
 #pragma unroll 1
           for (int c = c_lo; c < c_hi; ++c) {
@@ -1010,8 +1074,12 @@ cudaError_t launch_gemm_tc(const void* x, int64_t ldx, const int32_t* qweight,
                            const int32_t* qzeros, const void* scales, void* out, int64_t ldo,
                            int M, int N, int K, int group_size, int num_sms, int* dev_status,
                            cudaStream_t stream, const char** why, const void* bias,
-                           void* workspace, size_t workspace_bytes) {
+                           void* workspace, size_t workspace_bytes, bool silu) {
   *why = nullptr;
+  if (silu && (N % (2 * BN) || bias)) {
+    *why = "SiLU-mul epilogue needs N % 512 == 0 and no bias";
+    return cudaSuccess;
+  }
   if (!tc_supported(x, ldx, qweight, qzeros, scales, M, N, K, group_size)) {
     *why = "shape or alignment not supported";
     return cudaSuccess;
@@ -1027,11 +1095,11 @@ cudaError_t launch_gemm_tc(const void* x, int64_t ldx, const int32_t* qweight,
   bool ok = make_map_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, K, M, (uint64_t)ldx * 2, BK, BM,
                         CU_TENSOR_MAP_SWIZZLE_128B) &&
             make_map_2d(&tmW, CU_TENSOR_MAP_DATA_TYPE_INT32, qweight, N / 8, K, (uint64_t)N / 2,
-                        BN / 8, BK, CU_TENSOR_MAP_SWIZZLE_NONE) &&
-            make_map_2d(&tmS, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, scales, N, G, (uint64_t)N * 2, BN, 1,
-                        CU_TENSOR_MAP_SWIZZLE_NONE) &&
+                        (silu ? BN / 16 : BN / 8), BK, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+            make_map_2d(&tmS, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, scales, N, G, (uint64_t)N * 2,
+                        (silu ? BN / 2 : BN), 1, CU_TENSOR_MAP_SWIZZLE_NONE) &&
             make_map_2d(&tmZ, CU_TENSOR_MAP_DATA_TYPE_INT32, qzeros, N / 8, G, (uint64_t)N / 2,
-                        BN / 8, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
+                        (silu ? BN / 16 : BN / 8), 1, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (!ok) {
     *why = "cuTensorMapEncodeTiled failed";
     return cudaSuccess;
@@ -1055,7 +1123,8 @@ cudaError_t launch_gemm_tc(const void* x, int64_t ldx, const int32_t* qweight,
   a.bias = static_cast<const __half*>(bias);
   // split-K or stream-K when the caller's workspace holds the partials (after the decode
   // kernels' counter region, which must stay zero); otherwise one CTA per tile
-  a.splits = tc_splits(M, N, K, num_sms);
+  a.splits = silu ? 1 : tc_splits(M, N, K, num_sms);
+  a.silu = silu ? 1 : 0;
   a.part = nullptr;
   a.streamk = 0;
   a.tiles_n = (N + BN - 1) / BN;
@@ -1076,7 +1145,7 @@ cudaError_t launch_gemm_tc(const void* x, int64_t ldx, const int32_t* qweight,
   }
   dim3 grid((M + BM - 1) / BM, (N + BN - 1) / BN, a.splits);
   int sk_split = 0;
-  const int64_t sk_tiles = a.splits == 1 ? tc_streamk_plan(M, N, K, num_sms, &sk_split) : 0;
+  const int64_t sk_tiles = a.splits == 1 && !silu ? tc_streamk_plan(M, N, K, num_sms, &sk_split) : 0;
   if (sk_tiles > 0 && ws_ok) {
     a.streamk = 1;
     a.sk_tiles = (int)sk_tiles;

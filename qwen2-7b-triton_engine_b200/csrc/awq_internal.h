@@ -140,7 +140,8 @@ cudaError_t launch_gemm_tc(const void* x, int64_t ldx, const int32_t* qweight,
                            const int32_t* qzeros, const void* scales, void* out, int64_t ldo,
                            int M, int N, int K, int group_size, int num_sms, int* dev_status,
                            cudaStream_t stream, const char** why, const void* bias = nullptr,
-                           void* workspace = nullptr, size_t workspace_bytes = 0);
+                           void* workspace = nullptr, size_t workspace_bytes = 0,
+                           bool silu = false);
 // Split-K factor of the tcgen05 kernel and the workspace its fp32 partials need (0: none).
 // With less workspace than this the kernel runs one CTA per output tile.
 int tc_splits(int64_t M, int64_t N, int64_t K, int num_sms);

@@ -125,3 +125,28 @@ def test_silu_mul_golden(silu_golden, cuda):
         ref = c["out_bits"].view(np.float16).astype(np.float32)
         assert O.max_rel_err(h.float().cpu().numpy(), ref) <= TOL, name
     assert awq_b200.device_status() == 0
+
+
+@pytest.mark.parametrize("M,K,N", [
+    (40, 1024, 37888),      # 128-row tiles: 1 x 74 tile pairs of 128 gate + 128 up columns
+    (300, 512, 37888),      # 256-row tiles: 2 x 74, persistent CTAs
+    (1000, 512, 20480),     # 4 x 40, ragged last row tile
+])
+def test_silu_mul_tcgen05_epilogue(cuda, M, K, N):
+    """Above 16 tokens the tcgen05 kernel applies the SiLU-mul in its epilogue (each tile
+    holds 128 gate columns and the matching 128 up columns; only [M, N/2] is written):
+    against the CPU oracle, the reference MLP's sequence on this library's product, and
+    bit-equal on a repeated call."""
+    import awq_b200
+    qw, qz, s = O.make_awq_layer(K, N, 128, seed=M + 3)
+    x = O.make_x(M, K, seed=K + 5)
+    dx, dqw, dqz, ds = _dev(cuda, x, qw, qz, s)
+    a = awq_b200.gemm_silu_mul(dx, dqw, dqz, ds, 128)
+    b = awq_b200.gemm_silu_mul(dx, dqw, dqz, ds, 128)
+    torch.cuda.synchronize()
+    assert a.shape == (M, N // 2)
+    assert torch.equal(a, b)
+    assert O.max_rel_err(a.float().cpu().numpy(), O.awq_silu_mul_f32(x, qw, qz, s, 128)) <= TOL
+    seq = _sequence(awq_b200, dx, dqw, dqz, ds, 128)
+    assert O.max_rel_err(a.float().cpu().numpy(), seq.float().cpu().numpy()) <= TOL_SEQ
+    assert awq_b200.device_status() == 0
