@@ -156,6 +156,22 @@ AWQ_API int awq_gemm_f16_noalloc(const void* x, int64_t ldx, const int32_t* qwei
                                  const int32_t* qzeros, const void* scales, void* out, int64_t ldo,
                                  int64_t M, int64_t N, int64_t K, int64_t group_size, void* stream);
 
+/*
+ * The schedule the tcgen05 prefill kernel takes for an M x N x K product on a GPU with
+ * num_sms SMs, when the caller's workspace holds what it needs: *kind = AWQ_TC_GRID (one
+ * CTA per 256-column output tile, *param = tiles), AWQ_TC_PERSISTENT (more tiles than
+ * SMs: one CTA per SM takes tiles in turn, *param = tiles), AWQ_TC_STREAMK (tiles fill
+ * half to most of the SMs: *param = K/64 steps each tile's own CTA runs before the other
+ * CTAs share the tails) or AWQ_TC_SPLITK (*param = CTAs along K per tile).  Host-only
+ * arithmetic: needs no GPU.  No counterpart in the reference (introspection for tests
+ * and tuning).
+ */
+#define AWQ_TC_GRID 0
+#define AWQ_TC_PERSISTENT 1
+#define AWQ_TC_STREAMK 2
+#define AWQ_TC_SPLITK 3
+AWQ_API int awq_tc_schedule(int64_t M, int64_t N, int64_t K, int num_sms, int* kind, int* param);
+
 /* 1 if AWQ_PATH_TC can run this shape with these pointers, else 0. */
 AWQ_API int awq_tc_supported(const void* x, int64_t ldx, const int32_t* qweight, const int32_t* qzeros,
                      const void* scales, int64_t M, int64_t N, int64_t K, int64_t group_size);

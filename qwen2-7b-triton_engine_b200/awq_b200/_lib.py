@@ -43,6 +43,7 @@ SIGNATURES = {
     "awq_gemm_f16_bias": ([_P, _I64, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _SZ,
                            _P], _INT),
     "awq_tc_supported": ([_P, _I64, _P, _P, _P, _I64, _I64, _I64, _I64], _INT),
+    "awq_tc_schedule": ([_I64, _I64, _I64, _INT, _P, _P], _INT),
     "awq_device_status": ([_P, ctypes.POINTER(ctypes.c_int)], _INT),
     "awq_tp_comm_create": ([_INT, _INT, _I64, _P, ctypes.POINTER(_P)], _INT),
     "awq_tp_comm_open": ([_P, _P], _INT),

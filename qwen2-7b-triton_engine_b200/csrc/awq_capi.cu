@@ -153,6 +153,31 @@ int awq_workspace_init(void* workspace, size_t workspace_bytes, void* stream) {
   return AWQ_OK;
 }
 
+int awq_tc_schedule(int64_t M, int64_t N, int64_t K, int num_sms, int* kind, int* param) {
+  if (!kind || !param) return fail(AWQ_ERR_INVALID_ARG, "null kind or param");
+  if (M <= 0 || N <= 0 || K < 64 || K % 64 || num_sms <= 0 || M > (int64_t)1 << 30 ||
+      N > (int64_t)1 << 30 || K > (int64_t)1 << 30)
+    return fail(AWQ_ERR_INVALID_ARG, "M=%lld N=%lld K=%lld num_sms=%d out of range", (long long)M,
+                (long long)N, (long long)K, num_sms);
+  const int s = awq::tc_splits(M, N, K, num_sms);
+  if (s > 1) {
+    *kind = AWQ_TC_SPLITK;
+    *param = s;
+    return AWQ_OK;
+  }
+  int split = 0;
+  if (awq::tc_streamk_plan(M, N, K, num_sms, &split) > 0) {
+    *kind = AWQ_TC_STREAMK;
+    *param = split;
+    return AWQ_OK;
+  }
+  const int64_t bm = M > 128 ? 256 : 128;
+  const int64_t tiles = ((M + bm - 1) / bm) * ((N + 255) / 256);
+  *kind = tiles > num_sms ? AWQ_TC_PERSISTENT : AWQ_TC_GRID;
+  *param = (int)tiles;
+  return AWQ_OK;
+}
+
 int awq_tc_supported(const void* x, int64_t ldx, const int32_t* qweight, const int32_t* qzeros,
                      const void* scales, int64_t M, int64_t N, int64_t K, int64_t group_size) {
   return awq::tc_supported(x, ldx, qweight, qzeros, scales, M, N, K, group_size) ? 1 : 0;

@@ -145,6 +145,9 @@ cudaError_t launch_gemm_tc(const void* x, int64_t ldx, const int32_t* qweight,
 // Split-K factor of the tcgen05 kernel and the workspace its fp32 partials need (0: none).
 // With less workspace than this the kernel runs one CTA per output tile.
 int tc_splits(int64_t M, int64_t N, int64_t K, int num_sms);
+// Stream-K plan of the tcgen05 kernel: the tiles (0: not used) and, in *split, the K steps
+// each tile CTA runs before the other CTAs share the tails.
+int64_t tc_streamk_plan(int64_t M, int64_t N, int64_t K, int num_sms, int* split);
 size_t tc_workspace_bytes(int64_t M, int64_t N, int64_t K, int num_sms);
 
 // ---- small-M GEMM on tcgen05 with the dequantized weights in TMEM (awq_gemm_tc.cu) ----
