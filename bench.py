@@ -676,10 +676,11 @@ def mlp_block_bench(torch, awq_b200, dev, world, rank, comm):
     """the Qwen2-7B MLP (model/qwen2.py:181-196: gate+up with SiLU-mul,
     then down) at M = 1 and 512 over `world` GPUs through awq_b200.tp.TensorParallelMLP:
     gate+up split by columns in whole groups, down by the matching rows, the down output
-    summed over the ranks (the fused all-reduce kernel where it runs the call, else NCCL).
-    Also, per call, the rank's down product alone, the same product fused with its
-    all-reduce, and the product followed by an NCCL all-reduce of the [M, 3584] fp16
-    output: the all-reduce's cost is the difference."""
+    summed over the ranks (up to 16 tokens the fused decode kernel, above the prefill
+    product and the library's all-reduce kernel over NVLink; NCCL where neither runs).
+    Also, per call, the rank's down product alone, the same product with the library's
+    all-reduce (`down_fused_allreduce_us`), and the product followed by an NCCL
+    all-reduce of the [M, 3584] fp16 output: the all-reduce's cost is the difference."""
     import torch.distributed as dist
 
     from awq_b200 import tp
@@ -714,7 +715,9 @@ def mlp_block_bench(torch, awq_b200, dev, world, rank, comm):
             n_ms = _dev_time_ms(torch, dev, world, prod_nccl, 20, False)
             row["down_nccl_allreduce_us"] = round(n_ms * 1e3, 2)
             row["nccl_allreduce_cost_us"] = round((n_ms - prod_ms) * 1e3, 2)
-            row["block_allreduce"] = "fused" if mlp.down.fused_for(M) else "nccl"
+            row["block_allreduce"] = (("fused decode kernel" if M <= 16 else
+                                       "prefill product + NVLink all-reduce kernel")
+                                      if mlp.down.fused_for(M) else "nccl")
         out[f"M{M}"] = row
     st = awq_b200.device_status()
     out["device_status"] = st

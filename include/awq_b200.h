@@ -209,6 +209,14 @@ AWQ_API int awq_device_status(void* stream, int* status_out);
  * Every rank must then issue the same sequence of awq_gemm_f16_allreduce calls, in one
  * stream per communicator (CUDA-graph capture is fine).  awq_tp_comm_destroy after the
  * device has finished all calls.  max_n bounds N of the calls (multiple of 8).
+ *
+ * Above 16 tokens (communicators made by awq_tp_comm_create_ex with max_rows >= M) the
+ * product runs on the prefill kernels into an fp16 plane of this rank's buffer, and one
+ * all-reduce kernel follows over NVLink: each rank sums its 1/world row slice of every
+ * rank's plane in rank order (fp32 accumulation of the fp16 partials, one rounding),
+ * stores it into every rank's result plane, and copies the result plane to out once all
+ * slices are in -- the same bits on every rank, no NCCL.  Flags carry the call number,
+ * as above; the same time-out and reset rules apply.
  */
 typedef struct awq_tp_comm awq_tp_comm;
 #define AWQ_IPC_HANDLE_BYTES 64
@@ -216,6 +224,11 @@ typedef struct awq_tp_comm awq_tp_comm;
 
 AWQ_API int awq_tp_comm_create(int world, int rank, int64_t max_n, void* handle_out,
                                awq_tp_comm** comm_out);
+/* awq_tp_comm_create with room for calls of up to max_rows tokens above 16 (two fp16
+ * planes of max_rows x max_n more per rank; max_rows = 0 is awq_tp_comm_create).  No
+ * counterpart in the reference. */
+AWQ_API int awq_tp_comm_create_ex(int world, int rank, int64_t max_n, int64_t max_rows,
+                                  void* handle_out, awq_tp_comm** comm_out);
 AWQ_API int awq_tp_comm_open(awq_tp_comm* comm, const void* handles);
 /* Longest wait for the other ranks' tiles, in ns (default 2 s); then status bit 4. */
 AWQ_API int awq_tp_comm_set_timeout(awq_tp_comm* comm, uint64_t timeout_ns);
@@ -230,9 +243,10 @@ AWQ_API int awq_tp_comm_set_timeout(awq_tp_comm* comm, uint64_t timeout_ns);
 AWQ_API int awq_tp_comm_reset(awq_tp_comm* comm);
 AWQ_API int awq_tp_comm_destroy(awq_tp_comm* comm);
 
-/* 1 if awq_gemm_f16_allreduce can run this call (the decode kernel with one CTA per SM
- * in a single wave: N % 32 == 0, group_size % 64 == 0, 16-byte aligned qweight and x,
- * ldx % 8 == 0, N <= max_n), else 0.  Otherwise use awq_gemm_f16 + an all-reduce. */
+/* 1 if awq_gemm_f16_allreduce can run this call, else 0 (then use awq_gemm_f16 + an
+ * all-reduce).  M <= 16: the decode kernel with one CTA per SM in a single wave (N % 32
+ * == 0, group_size % 64 == 0, 16-byte aligned qweight and x, ldx % 8 == 0, N <= max_n).
+ * M > 16: M <= the communicator's max_rows and N <= max_n. */
 AWQ_API int awq_allreduce_supported(const awq_tp_comm* comm, const void* x, int64_t ldx,
                                     const int32_t* qweight, int64_t M, int64_t N, int64_t K,
                                     int64_t group_size);

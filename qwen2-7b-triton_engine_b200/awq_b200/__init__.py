@@ -315,22 +315,26 @@ class TPComm:
     buffer on this rank's GPU that every other rank maps through CUDA IPC and writes its
     tile results into over NVLink.
 
-    ``TPComm(world, rank, max_n)`` allocates the buffer on the current device and exposes
-    ``handle`` (bytes); ``open(handles)`` takes every rank's handle in rank order.
-    ``TPComm.from_group(max_n, group)`` does both with ``torch.distributed``.  All ranks
-    must then issue the same sequence of ``gemm_allreduce`` calls, one stream per
-    communicator.  ``close()`` after the device has finished those calls."""
+    ``TPComm(world, rank, max_n, max_rows=2048)`` allocates the buffer on the current
+    device and exposes ``handle`` (bytes); ``open(handles)`` takes every rank's handle in
+    rank order.  ``TPComm.from_group(max_n, group)`` does both with ``torch.distributed``.
+    All ranks must then issue the same sequence of ``gemm_allreduce`` calls, one stream
+    per communicator.  ``close()`` after the device has finished those calls.  Calls of
+    up to 16 tokens run the fused decode kernel; calls of 17 to ``max_rows`` tokens run
+    the prefill product into the buffer and the library's all-reduce kernel over NVLink
+    (two fp16 planes of ``max_rows x max_n`` per rank; ``max_rows=0`` leaves them out)."""
 
-    def __init__(self, world: int, rank: int, max_n: int, device=None):
+    def __init__(self, world: int, rank: int, max_n: int, device=None, max_rows: int = 2048):
         self.device = torch.device("cuda", torch.cuda.current_device()) if device is None \
             else torch.device(device)
         self.world, self.rank, self.max_n = int(world), int(rank), int(max_n)
+        self.max_rows = int(max_rows)
         lib = _lib.load()
         h = ctypes.create_string_buffer(_lib.AWQ_IPC_HANDLE_BYTES)
         ptr = ctypes.c_void_p()
         with _DeviceGuard(self.device):
-            _lib.check(lib.awq_tp_comm_create(self.world, self.rank, self.max_n, h,
-                                              ctypes.byref(ptr)))
+            _lib.check(lib.awq_tp_comm_create_ex(self.world, self.rank, self.max_n,
+                                                 self.max_rows, h, ctypes.byref(ptr)))
         self._ptr = ptr
         self.handle = h.raw
         self.opened = False
@@ -344,12 +348,16 @@ class TPComm:
         self.opened = True
 
     @classmethod
-    def from_group(cls, max_n: int, group=None, device=None) -> "TPComm":
+    def from_group(cls, max_n: int, group=None, device=None, max_rows: int = 2048) -> "TPComm":
         import torch.distributed as dist
-        comm = cls(dist.get_world_size(group), dist.get_rank(group), max_n, device)
-        handles = [None] * comm.world
-        dist.all_gather_object(handles, comm.handle, group=group)
-        comm.open(handles)
+        comm = cls(dist.get_world_size(group), dist.get_rank(group), max_n, device, max_rows)
+        got = [None] * comm.world
+        dist.all_gather_object(got, (comm.handle, comm.max_n, comm.max_rows), group=group)
+        # every rank's buffer must have the same layout: the ranks store into each other's
+        if any(g[1:] != (comm.max_n, comm.max_rows) for g in got):
+            comm.close()
+            raise ValueError(f"ranks disagree on (max_n, max_rows): {[g[1:] for g in got]}")
+        comm.open([g[0] for g in got])
         dist.barrier(group=group)
         return comm
 

@@ -46,6 +46,7 @@ SIGNATURES = {
     "awq_tc_schedule": ([_I64, _I64, _I64, _INT, _P, _P], _INT),
     "awq_device_status": ([_P, ctypes.POINTER(ctypes.c_int)], _INT),
     "awq_tp_comm_create": ([_INT, _INT, _I64, _P, ctypes.POINTER(_P)], _INT),
+    "awq_tp_comm_create_ex": ([_INT, _INT, _I64, _I64, _P, ctypes.POINTER(_P)], _INT),
     "awq_tp_comm_open": ([_P, _P], _INT),
     "awq_tp_comm_set_timeout": ([_P, ctypes.c_uint64], _INT),
     "awq_tp_comm_reset": ([_P], _INT),

@@ -192,11 +192,12 @@ class RowParallelAWQ:
         self._fused_ok: dict = {}
 
     def fused_for(self, M: int) -> bool:
-        """Whether a call with M activation rows runs the fused kernel (the same answer on
-        every rank: it depends on M, N, the group size and every rank's K only).  The
-        fused kernel is the decode kernel, so it takes decode-sized calls (M <= 16); larger
-        M runs the prefill GEMM and NCCL."""
-        if self.comm is None or self.world < 2 or self.k_all is None or M > 16:
+        """Whether a call with M activation rows runs the library's all-reduce (the same
+        answer on every rank: it depends on M, N, the group size, every rank's K and the
+        communicator's capacity only).  Up to 16 tokens that is the fused decode kernel;
+        above, the prefill product followed by the all-reduce kernel, up to the
+        communicator's ``max_rows``; beyond that, the product and NCCL."""
+        if self.comm is None or self.world < 2 or self.k_all is None:
             return False
         ok = self._fused_ok.get(M)
         if ok is None:

@@ -425,6 +425,7 @@ int awq_allreduce_supported(const awq_tp_comm* comm, const void* x, int64_t ldx,
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev != comm->device) return 0;
   if (M <= 0 || N <= 0 || N > comm->max_n || group_size <= 0 || K <= 0 || K % group_size) return 0;
+  if (M > 16) return M <= comm->max_rows && N <= comm->max_n && N % 8 == 0 ? 1 : 0;
   if (!awq::gemv_tma_supported(qweight, N, ldx, x)) return 0;
   // every launch must run its CTAs in one wave: a tile's last CTA waits for the other
   // ranks, and must never hold an SM that a not-yet-started CTA of its own grid needs
@@ -455,6 +456,19 @@ int awq_gemm_f16_allreduce(awq_tp_comm* comm, const void* x, int64_t ldx, const 
                 (long long)group_size);
   DeviceInfo* d = nullptr;
   if ((rc = device_info(&d))) return rc;
+  if (M > 16) {
+    // prefill-sized: the product into this rank's plane, then the all-reduce kernel
+    if (!aligned16(out) || ldo % 8)
+      return fail(AWQ_ERR_INVALID_ARG, "out must be 16-byte aligned with ldo %% 8 == 0 above 16 tokens");
+    void* plane = awq::tp_big_in_plane(comm);
+    rc = gemm_impl(x, ldx, qweight, qzeros, scales, plane, N, M, N, K, group_size, workspace,
+                   workspace_bytes, stream, AWQ_PATH_AUTO, nullptr);
+    if (rc) return rc;
+    cudaError_t e = awq::launch_tp_big_allreduce(comm, (int)M, (int)N, out, ldo, d->num_sms,
+                                                 d->status, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return fail_cuda(e, "all-reduce kernel launch");
+    return AWQ_OK;
+  }
   awq::ArArgs ar;
   if (!awq::tp_ar_args(comm, &ar)) return fail(AWQ_ERR_INVALID_ARG, "communicator not opened");
   awq::GemvTmaPlan full = {}, rest = {};

@@ -169,11 +169,33 @@ inline size_t tp_buffer_bytes(int world, int max_tiles) {
   return tp_data_offset() + (size_t)2 * world * max_tiles * kArTileFloats * 8;
 }
 
+// All-reduce of prefill-sized outputs (M > 16; communicators made with max_rows > 0).
+// After the decode region come two fp16 planes of [max_rows][max_n]: `in`, where this
+// rank's product kernel writes its partial output, and `res`, where the owner of each
+// row slice (rank r owns rows [M r / world, M (r + 1) / world)) writes the summed rows.
+// In the header: state words at kBigStateOffset ([0] calls so far, [1] CTAs past their
+// slice this call, [2] CTAs done this call) and flags at kBigFlagOffset (in_flag[world]
+// then res_flag[world], written by the other ranks: the call number + 1 of the latest
+// call whose input / summed slice that rank has published).
+constexpr size_t kBigStateOffset = 64, kBigFlagOffset = 128;
+inline size_t tp_big_offset(int world, int max_tiles) {
+  return (tp_buffer_bytes(world, max_tiles) + 255) / 256 * 256;
+}
+inline size_t tp_big_plane_bytes(int64_t max_rows, int64_t max_n) {
+  return ((size_t)max_rows * max_n * 2 + 255) / 256 * 256;
+}
+
 }  // namespace awq
 struct awq_tp_comm;
 namespace awq {
 // Kernel arguments of a ready communicator (false when it is not opened).
 bool tp_ar_args(const awq_tp_comm* comm, ArArgs* args);
+// This rank's `in` plane (null when the communicator has no prefill region), and the
+// all-reduce of the fp16 [M, N] partials the ranks wrote there into out (row stride
+// ldo): reduce-scatter by row slices, all-gather through the `res` planes.
+void* tp_big_in_plane(const awq_tp_comm* comm);
+cudaError_t launch_tp_big_allreduce(const awq_tp_comm* comm, int M, int N, void* out, int64_t ldo,
+                                    int num_sms, int* dev_status, cudaStream_t stream);
 
 // Sets the message awq_last_error() returns on this thread; returns `code`.
 int set_last_error(int code, const char* msg);
@@ -184,6 +206,7 @@ int set_last_error(int code, const char* msg);
 struct awq_tp_comm {
   int device = 0, world = 1, rank = 0;
   int64_t max_n = 0;
+  int64_t max_rows = 0;                    // rows of the prefill all-reduce planes (0: none)
   int max_tiles = 0;
   size_t bytes = 0;
   void* local = nullptr;                   // this rank's receive buffer

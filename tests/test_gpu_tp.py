@@ -138,7 +138,7 @@ def test_tp_world2_matches_single_gpu(cuda, M):
         assert O.max_rel_err(z, z_ref) <= TOL, rank
 
 
-def _fused_worker(rank, world, port, Ms, seed, q):
+def _fused_worker(rank, world, port, Ms, seed, q, chain_M=1):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
@@ -170,7 +170,7 @@ def _fused_worker(rank, world, port, Ms, seed, q):
             res[M] = (z.cpu().numpy(), y.cpu().numpy())
         # a chain of fused calls replayed from a CUDA graph: o, then down on o's output
         # (tiled to INTER columns), 3 times, against the same chain run eagerly
-        x = torch.from_numpy(O.make_x(1, HIDDEN, seed=seed + 5)).to(dev)
+        x = torch.from_numpy(O.make_x(chain_M, HIDDEN, seed=seed + 5)).to(dev)
 
         def chain():
             v = x
@@ -222,6 +222,11 @@ def test_fused_allreduce_world2_matches_single_gpu_and_ranks_agree(cuda):
     port = _free_port()
     procs = [ctx.Process(target=_fused_worker, args=(r, world, port, Ms, seed, q)) for r in range(world)]
     _start(procs, world)
+    _check_fused(cuda, q, procs, world, Ms, seed)
+
+
+def _check_fused(cuda, q, procs, world, Ms, seed):
+    import awq_b200
     got = {}
     for rank, res, eager, graphed, st in _collect(q, procs, world):
         got[rank] = (res, eager, graphed, st)
@@ -246,6 +251,27 @@ def test_fused_allreduce_world2_matches_single_gpu_and_ranks_agree(cuda):
         assert st == 0
         assert np.array_equal(eager, graphed)
     assert np.array_equal(got[0][1], got[1][1])
+
+
+def test_prefill_allreduce_world2_matches_single_gpu_and_ranks_agree(cuda):
+    """Row-parallel o and down above 16 tokens on 2 GPUs: each rank's prefill product goes
+    into its communicator plane, and the library's all-reduce kernel sums the row slices
+    over NVLink (reduce-scatter, then all-gather through the other rank's plane; no
+    NCCL).  Equal to the single-GPU product within the tolerance, bit-identical on both
+    ranks, ragged slices (M = 17, 100), and a graph-replayed chain of 48-token calls
+    gives the eager chain's bits (the call numbers in the flags advance on replay)."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from conftest import PKG, REPO
+    world, seed, Ms = 2, 37, (17, 100, 512)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    os.environ.update(AWQ_PKG=str(PKG), AWQ_REPO=str(REPO))
+    port = _free_port()
+    procs = [ctx.Process(target=_fused_worker, args=(r, world, port, Ms, seed, q, 48))
+             for r in range(world)]
+    _start(procs, world)
+    _check_fused(cuda, q, procs, world, Ms, seed)
 
 
 def _recovery_worker(rank, world, port, seed, q):

@@ -1,7 +1,9 @@
 """GPU, one device: the fused row-parallel all-reduce's wait for other ranks is bounded.
 
 A world of 2 is built inside this process (two communicators on one GPU, each opening
-the other's buffer); only rank 0 calls, so its wait for rank 1's tiles can never end.
+the other's buffer); only rank 0 calls, so its wait for rank 1's tiles (M = 1: the fused
+decode kernel) or rank 1's partial and row slice (M = 48: the all-reduce kernel after the
+prefill product) can never end.
 The kernel must give up after the communicator's time-out, set status bit 4 and finish
 -- no hang, no fault -- and the library must keep working afterwards.  Nothing runs on
 a second device and no kernel waits on another kernel of this GPU.
@@ -19,7 +21,8 @@ from oracle import oracle as O
 pytestmark = pytest.mark.gpu
 
 
-def test_fused_allreduce_wait_times_out_with_status(cuda):
+@pytest.mark.parametrize("M", [1, 48])
+def test_fused_allreduce_wait_times_out_with_status(cuda, M):
     import awq_b200
     import awq_b200._lib as L
     K, N = 1024, 512
@@ -30,7 +33,7 @@ def test_fused_allreduce_wait_times_out_with_status(cuda):
         c1.open([c0.handle, c1.handle])
         c0.set_timeout(0.05)
         qw, qz, s = (torch.from_numpy(a).to(cuda) for a in O.make_awq_layer(K, N, 128, seed=4))
-        x = torch.from_numpy(O.make_x(1, K, seed=4)).to(cuda)
+        x = torch.from_numpy(O.make_x(M, K, seed=4)).to(cuda)
         assert c0.supported(x, qw, N)
         torch.cuda.synchronize()
         t0 = time.perf_counter()
@@ -60,14 +63,15 @@ def test_fused_allreduce_wait_times_out_with_status(cuda):
         c0.close()
 
 
-def test_world1_communicator_is_a_plain_product(cuda):
+@pytest.mark.parametrize("M", [3, 40])
+def test_world1_communicator_is_a_plain_product(cuda, M):
     import awq_b200
     K, N = 2048, 1024
     c = awq_b200.TPComm(1, 0, N)
     try:
         c.open([c.handle])
         qw, qz, s = (torch.from_numpy(a).to(cuda) for a in O.make_awq_layer(K, N, 128, seed=6))
-        x = torch.from_numpy(O.make_x(3, K, seed=6)).to(cuda)
+        x = torch.from_numpy(O.make_x(M, K, seed=6)).to(cuda)
         a = awq_b200.gemm_allreduce(x, qw, qz, s, 128, c)
         b = awq_b200.gemm(x, qw, qz, s, 128)
         torch.cuda.synchronize()
