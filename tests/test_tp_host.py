@@ -259,12 +259,17 @@ def test_attention_linears_by_heads_gloo_world4():
 
 # ---- the fused / NCCL choice of a row-parallel call is the same on every rank ----
 class _FakeComm:
-    """Stands in for awq_b200.TPComm on CPU ranks.  Its shape rule (K a multiple of 256,
-    M <= 16) makes ranks whose K differ answer differently on their own; the agreed
-    choice must still come out the same everywhere."""
+    """Stands in for awq_b200.TPComm on CPU ranks, with the library's rule in small: up
+    to 16 tokens the fused decode kernel, which needs K a multiple of 256 here (so ranks
+    whose K differ answer differently on their own); 17 to max_rows tokens the prefill
+    product and the all-reduce kernel, which any K takes; beyond that NCCL.  The agreed
+    choice must come out the same everywhere."""
+    max_rows = 128
 
     def supported_shape(self, M, N, K, group_size=128):
-        return K > 0 and K % 256 == 0 and M <= 16
+        if M > 16:
+            return K > 0 and M <= self.max_rows
+        return K > 0 and K % 256 == 0
 
 
 def _choice_worker(rank, world, port, K, q):
@@ -278,17 +283,18 @@ def _choice_worker(rank, world, port, K, q):
         o = _layer(K, 128, 7)
         ro = tp.RowParallelAWQ(tp.AWQWeights(*o), world, rank, gemm=_cpu_gemm, comm=_FakeComm())
         local = _FakeComm().supported_shape(1, 128, ro.k1 - ro.k0)
-        q.put((rank, ro.k1 - ro.k0, local, ro.fused_for(1), ro.fused_for(64)))
+        q.put((rank, ro.k1 - ro.k0, local, ro.fused_for(1), ro.fused_for(64),
+               ro.fused_for(512)))
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,K,want", [
-    (2, 512, True),      # 256 rows each: every rank can run the fused kernel
-    (2, 384, False),     # 256 and 128 rows: rank 1 cannot, so neither does
-    (4, 384, False),     # 3 groups over 4 ranks: the last rank holds no rows
+@pytest.mark.parametrize("world,K,want,want64", [
+    (2, 512, True, True),      # 256 rows each: every rank can run the fused kernel
+    (2, 384, False, True),     # 256 and 128 rows: rank 1 cannot, so neither does at M = 1
+    (4, 384, False, False),    # 3 groups over 4 ranks: the last rank holds no rows
 ])
-def test_row_parallel_fused_choice_agrees_across_ranks(world, K, want):
+def test_row_parallel_fused_choice_agrees_across_ranks(world, K, want, want64):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
@@ -300,7 +306,8 @@ def test_row_parallel_fused_choice_agrees_across_ranks(world, K, want):
         p.join(timeout=60)
         assert p.exitcode == 0
     assert {g[3] for g in got} == {want}           # M = 1: one decision, the expected one
-    assert {g[4] for g in got} == {False}          # M = 64 is beyond the fused kernel
+    assert {g[4] for g in got} == {want64}         # M = 64: product + all-reduce kernel
+    assert {g[5] for g in got} == {False}          # M = 512 > max_rows: NCCL
     if not want:
         # at least one rank would have chosen the fused kernel on its own K alone
         assert any(g[2] for g in got) or any(g[1] == 0 for g in got)
