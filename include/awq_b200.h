@@ -7,8 +7,9 @@
  * cudaStream_t (NULL = the legacy default stream).  The product entry points
  * allocate no device memory and never synchronize: they only enqueue kernels on
  * `stream`.  The exceptions are named where they are declared: the
- * tensor-parallel set-up and tear-down (awq_tp_comm_create / _open / _destroy)
- * allocate, map or free a buffer and synchronize the device, and
+ * tensor-parallel set-up and tear-down (awq_tp_comm_create / _create_ex / _open /
+ * _destroy) allocate, map or free a buffer and synchronize the device, awq_tp_comm_reset
+ * synchronizes the device, and
  * awq_device_status synchronizes `stream`.  Nothing throws; each entry point
  * returns AWQ_OK (0) or a negative AWQ_ERR_* code, and awq_last_error() gives a
  * message for the calling thread.
