@@ -26,16 +26,18 @@ with the benchmark's distributions (synthetic data; no checkpoint exists here).
 
   mlp       BASELINE config 4: the Qwen2-7B MLP block (gate+up with SiLU-mul, down) at
             M = 1 and 512 over the N GPUs (tensor parallel: gate+up by columns, down by
-            rows + all-reduce), with the row-parallel down's product alone, fused with its
-            all-reduce, and followed by NCCL, per call
+            rows + all-reduce), with the row-parallel down's product alone, with the
+            library's all-reduce (M = 1: one fused kernel; M = 512: product + the NVLink
+            all-reduce kernel), and followed by NCCL, per call
   stack     BASELINE config 5: the 28-layer linear stack with RMSNorm and residual adds
             between the linears, a 1024-token prefill and 512 graph-replayed decode
             steps at batch 1, tokens/s over the N GPUs
 
 With torchrun (N > 1) every rank runs the tensor-parallel stack: qkv and gate+up
 column-sharded, o and down row-sharded, each row-parallel call's fp16 output summed over
-the ranks by the fused all-reduce kernel where it runs the shape, else NCCL (strong
-scaling: the token's total bytes are fixed).
+the ranks by the library's all-reduce over NVLink peer memory (decode: fused into the
+product kernel; prefill: a separate all-reduce kernel after the product), else NCCL
+(strong scaling: the token's total bytes are fixed).
 ``--impl reference`` times the reference's own CPU path (oracle port) instead.
 ``--stack`` runs only the config-5 leg (see stack_bench).
 """
