@@ -185,3 +185,20 @@ def test_activation_and_output_checks_without_a_device():
     assert lib.awq_gemm_f16_bias(16, 256, *ok, None, 16, 64, 1, 64, 256, 128, None, 0, None) == \
         L.AWQ_ERR_INVALID_ARG
     assert b"bias" in lib.awq_last_error()
+
+
+def test_communicator_create_rejects_bad_arguments_without_a_device():
+    """awq_tp_comm_create_ex validates world, rank, max_n and max_rows before it touches
+    CUDA: a bad request fails with AWQ_ERR_INVALID_ARG and leaves no communicator."""
+    import ctypes
+    import awq_b200._lib as L
+    lib = L.load()
+    h = ctypes.create_string_buffer(L.AWQ_IPC_HANDLE_BYTES)
+    for world, rank, max_n, max_rows in [(0, 0, 256, 0), (9, 0, 256, 0), (2, 2, 256, 0),
+                                         (2, 0, 100, 0), (2, 0, 256, -1),
+                                         (2, 0, 1 << 16, 1 << 17)]:
+        ptr = ctypes.c_void_p(1)
+        rc = lib.awq_tp_comm_create_ex(world, rank, max_n, max_rows, h, ctypes.byref(ptr))
+        assert rc == L.AWQ_ERR_INVALID_ARG, (world, rank, max_n, max_rows)
+        assert ptr.value is None
+    assert lib.awq_tp_comm_create_ex(2, 0, 256, 0, None, None) == L.AWQ_ERR_INVALID_ARG
