@@ -25,10 +25,10 @@ with the benchmark's distributions (synthetic data; no checkpoint exists here).
             torch on every host core) on one layer's 4 linears at M=1
 
   mlp       BASELINE config 4: the Qwen2-7B MLP block (gate+up with SiLU-mul, down) at
-            M = 1 and 512 over the N GPUs (tensor parallel: gate+up by columns, down by
-            rows + all-reduce), with the row-parallel down's product alone, with the
-            library's all-reduce (M = 1: one fused kernel; M = 512: product + the NVLink
-            all-reduce kernel), and followed by NCCL, per call
+            M = 1, 16 and 512 over the N GPUs (tensor parallel: gate+up by columns, down
+            by rows + all-reduce), with the row-parallel down's product alone, with the
+            library's all-reduce (M <= 16: one fused kernel; M = 512: product + the
+            NVLink all-reduce kernel), and followed by NCCL, per call
   stack     BASELINE config 5: the 28-layer linear stack with RMSNorm and residual adds
             between the linears, a 1024-token prefill and 512 graph-replayed decode
             steps at batch 1, tokens/s over the N GPUs
@@ -676,7 +676,7 @@ def _dev_time_ms(torch, dev, world, fn, reps, graph):
 
 def mlp_block_bench(torch, awq_b200, dev, world, rank, comm):
     """the Qwen2-7B MLP (model/qwen2.py:181-196: gate+up with SiLU-mul,
-    then down) at M = 1 and 512 over `world` GPUs through awq_b200.tp.TensorParallelMLP:
+    then down) at M = 1, 16 and 512 over `world` GPUs through awq_b200.tp.TensorParallelMLP:
     gate+up split by columns in whole groups, down by the matching rows, the down output
     summed over the ranks (up to 16 tokens the fused decode kernel, above the prefill
     product and the library's all-reduce kernel over NVLink; NCCL where neither runs).
@@ -695,7 +695,7 @@ def mlp_block_bench(torch, awq_b200, dev, world, rank, comm):
     out = {"what": "TensorParallelMLP: gate+up (SiLU-mul fused) and down, all-reduce of the "
                    "down output across the ranks", "n_gpus": world}
     w = mlp.down.w
-    for M in (1, 512):
+    for M in (1, 16, 512):
         x = torch.randn((M, HIDDEN), device=dev, generator=gen).half()
         graph = M <= 16                    # decode: replayed from a CUDA graph
         ms = _dev_time_ms(torch, dev, world, lambda: mlp(x), 20 if graph else 5, graph)

@@ -123,8 +123,9 @@ AWQ_API int awq_gemm_f16_bias(const void* x, int64_t ldx, const int32_t* qweight
  * (model/qwen2.py:181-194, kernels/silu_mul.py:41-64): fp16-rounded G and U, fp32
  * x * sigmoid(x) * y, one fp16 rounding.  Up to 8 tokens with N/2 a multiple of 256 the
  * decode kernel pairs each gate strip with its up strip in its epilogue (P is never
- * written); otherwise the product goes to a temporary inside the workspace and one
- * elementwise kernel follows.  Workspace: awq_gemm_silu_mul_workspace_bytes bytes,
+ * written); from 9 tokens up, with N a multiple of 512 and enough output tiles to run
+ * without a K split, the tcgen05 kernels do the same in theirs; otherwise the product
+ * goes to a temporary inside the workspace and one elementwise kernel follows.  Workspace: awq_gemm_silu_mul_workspace_bytes bytes,
  * zero-filled once (awq_workspace_init), the same buffer the other calls use.
  */
 AWQ_API size_t awq_gemm_silu_mul_workspace_bytes(int64_t M, int64_t N, int64_t K,

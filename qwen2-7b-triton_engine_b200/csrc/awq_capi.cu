@@ -379,6 +379,20 @@ int awq_gemm_f16_silu_mul(const void* x, int64_t ldx, const int32_t* qweight,
     if (e != cudaSuccess) return fail_cuda(e, "decode (TMA) kernel launch, SiLU-mul epilogue");
     return AWQ_OK;
   }
+  // From 9 to 16 tokens the product runs on the small-M tcgen05 kernel; when it runs
+  // without a K split (every Qwen2-7B gate+up call), its epilogue does the SiLU-mul the
+  // same way: each CTA's 256 columns are 128 gate and the matching 128 up columns.
+  if (M > 8 && M <= 16 && N % 512 == 0 &&
+      awq::ts_supported(x, ldx, qweight, qzeros, scales, M, N, K, group_size) &&
+      awq::ts_splits(M, N, K, d->num_sms) == 1) {
+    const char* why = nullptr;
+    cudaError_t e = awq::launch_gemm_ts(x, ldx, qweight, qzeros, scales, out, ldo, (int)M,
+                                        (int)N, (int)K, (int)group_size, d->num_sms, d->status,
+                                        st, &why, nullptr, nullptr, 0, /*silu=*/true);
+    if (why) return fail(AWQ_ERR_UNSUPPORTED, "small-M tcgen05 SiLU-mul path: %s", why);
+    if (e != cudaSuccess) return fail_cuda(e, "small-M tcgen05 GEMM launch, SiLU-mul epilogue");
+    return AWQ_OK;
+  }
   // Above 16 tokens, when the product would run on the tcgen05 kernel unsplit (its tiles
   // fill at least half the SMs: every Qwen2-7B gate+up call), that kernel's epilogue does
   // the SiLU-mul: a tile holds 128 gate and the matching 128 up columns, and only the

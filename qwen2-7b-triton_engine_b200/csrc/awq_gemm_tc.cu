@@ -684,7 +684,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 // pairs).  Its 8 output slots are the 8 nibble slots u of the word: slot u goes to half
 // h = u / 4, lane 32 q + 8 (u % 4) + t1, and is element [0,2,4,6,1,3,5,7][u] of the word.
 // Lanes, halves and output columns map one to one; the epilogue inverts the map.
-constexpr int kTsAStages = 4;                    // TMEM A stages of 64 columns
+//
+// SiLU-mul mode (args.silu): packed words 0-15 of the tile are gate words, 16-31 the
+// matching up words, so lane quarter q + 2 holds the up column of quarter q's gate column
+// in the same lane and half; the epilogue pairs them through shared memory.
+constexpr int kTsAStages = 4;                   // TMEM A stages of 64 columns
 constexpr uint32_t kTsTmemCols = 512;
 constexpr uint32_t kTsDCol = kTsAStages * 64;    // accumulators: 2 halves x NT columns
 constexpr int kTsMinSteps = 4;                   // K steps per CTA at least (split-K)
@@ -702,6 +706,11 @@ struct TsGeo {
   static constexpr uint32_t OFF_MISC = OFF_BAR + NBARS * 8;
   static constexpr uint32_t SMEM_BYTES = OFF_MISC + 16 + 1024;
   static_assert(X_BYTES % 1024 == 0, "x tile must keep the weight tile 1 KB aligned");
+  // SiLU-mul mode: every TMA destination 128-byte aligned (the up half of the weight tile
+  // at T_RAW + 4 KB, of the scales at T_SC + 256, of the zeros at T_ZR + 128)
+  static_assert(T_SC % 128 == 0 && T_ZR % 128 == 0 && T_ZR + 128 + ZR_BYTES / 2 <= T_STAGE,
+                "SiLU-mul half boxes");
+  static_assert(NT * 128 * 4 <= TSTAGES * T_STAGE, "SiLU-mul epilogue exchange");
   static_assert(kTsDCol + 2 * NT <= kTsTmemCols, "TMEM columns");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
 };
@@ -779,9 +788,20 @@ gemm_ts_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
         const uint32_t st = sbase + s * T_STAGE;
         sm100::mbar_arrive_expect_tx(bar_tfull(s), TX_BYTES);
         sm100::tma_load_2d(st, &tmX, bar_tfull(s), k0, tile_m * NT);
-        sm100::tma_load_2d(st + T_RAW, &tmW, bar_tfull(s), tile_n * (BN / 8), k0);
-        sm100::tma_load_2d(st + T_SC, &tmS, bar_tfull(s), tile_n * BN, grp);
-        sm100::tma_load_2d(st + T_ZR, &tmZ, bar_tfull(s), tile_n * (BN / 8), grp);
+        if (args.silu) {
+          // gate words [16 n, 16 n + 16) and the same up words, N / 16 further on
+          const int gw = tile_n * (BN / 16), uw = args.N / 16 + gw;
+          sm100::tma_load_2d(st + T_RAW, &tmW, bar_tfull(s), gw, k0);
+          sm100::tma_load_2d(st + T_RAW + RAW_BYTES / 2, &tmW, bar_tfull(s), uw, k0);
+          sm100::tma_load_2d(st + T_SC, &tmS, bar_tfull(s), gw * 8, grp);
+          sm100::tma_load_2d(st + T_SC + SC_BYTES / 2, &tmS, bar_tfull(s), uw * 8, grp);
+          sm100::tma_load_2d(st + T_ZR, &tmZ, bar_tfull(s), gw, grp);
+          sm100::tma_load_2d(st + T_ZR + 128, &tmZ, bar_tfull(s), uw, grp);
+        } else {
+          sm100::tma_load_2d(st + T_RAW, &tmW, bar_tfull(s), tile_n * (BN / 8), k0);
+          sm100::tma_load_2d(st + T_SC, &tmS, bar_tfull(s), tile_n * BN, grp);
+          sm100::tma_load_2d(st + T_ZR, &tmZ, bar_tfull(s), tile_n * (BN / 8), grp);
+        }
       }
       for (int j = (kt > TSTAGES ? kt - TSTAGES : 0); j < kt; ++j)
         sm100::mbar_wait_bounded(bar_tfull(j % TSTAGES), (j / TSTAGES) & 1, args.status);
@@ -819,6 +839,25 @@ gemm_ts_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
     const int rb = ((warp - 2) >> 2) * 2;    // first of its two 16-row K blocks
     const int t0 = lane & 3, t1 = lane >> 2;
     const int wc = 8 * q + t1;               // packed word column within the tile
+    // Byte offsets of this thread's 8 packed words of a K step within the weight tile.
+    // One 32-word box: 128-byte rows, 128-byte swizzle (16-byte chunk ^= row % 8).
+    // SiLU-mul: two 16-word boxes (gate, then up 4 KB further), 64-byte rows, 64-byte
+    // swizzle (16-byte chunk ^= (row / 2) % 4).
+    uint32_t woff[2][4];
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t row = 16 * (rb + rr) + 4 * t0 + i;
+        woff[rr][i] = args.silu
+                          ? (uint32_t)(wc >> 4) * (RAW_BYTES / 2) + row * 64 +
+                                ((((uint32_t)(wc & 15) >> 2) ^ ((row >> 1) & 3)) << 4) +
+                                ((uint32_t)(wc & 3) << 2)
+                          : row * 128 + (((uint32_t)(wc >> 2) ^ (row & 7)) << 4) +
+                                ((uint32_t)(wc & 3) << 2);
+      }
+    const uint32_t zoff = args.silu ? (uint32_t)(wc >> 4) * 128u + 4u * (uint32_t)(wc & 15)
+                                    : 4u * (uint32_t)wc;
     uint32_t zc[8], sc[8];
     int grp_have = -1;
     for (int kt = 0; kt < KT; ++kt) {
@@ -838,7 +877,7 @@ gemm_ts_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
       const int grp = (kt0 + kt) * BK / args.gs;
       if (grp != grp_have) {
         grp_have = grp;
-        const uint32_t zw = reinterpret_cast<const uint32_t*>(tst + T_ZR)[wc];
+        const uint32_t zw = *reinterpret_cast<const uint32_t*>(tst + T_ZR + zoff);
         const uint4 s4 = reinterpret_cast<const uint4*>(tst + T_SC)[wc];
         const uint32_t sw[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
@@ -857,12 +896,8 @@ gemm_ts_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
       for (int rr = 0; rr < 2; ++rr) {
         uint32_t a[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int row = 16 * (rb + rr) + 4 * t0 + i;
-          const uint32_t addr = raw + row * 128 + ((uint32_t)((wc >> 2) ^ (row & 7)) << 4) +
-                                ((uint32_t)(wc & 3) << 2);
-          asm volatile("ld.shared.b32 %0, [%1];" : "=r"(a[i]) : "r"(addr));
-        }
+        for (int i = 0; i < 4; ++i)
+          asm volatile("ld.shared.b32 %0, [%1];" : "=r"(a[i]) : "r"(raw + woff[rr][i]));
 #pragma unroll
         for (int p = 0; p < 2; ++p) {
 #pragma unroll
@@ -898,7 +933,46 @@ gemm_ts_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
     // ------------------------------------------------------------- epilogue --------
     const bool ok = sm100::mbar_wait_bounded(bar_accf, 0, args.status);
     sm100::tc_fence_after();
-    if (ok && !*abort_flag) {
+    if (args.silu) {
+      // Lane quarters 2 and 3 hold the up columns of the gate columns in quarters 0 and 1
+      // (same lane, same half): they pass their fp32 sums through the ring's shared memory
+      // (every copy has landed and every MMA has read its operands once the accumulators
+      // are complete), laid out [token][column]; quarters 0 and 1 write
+      // out[m, 128 n + c] = fp16(silu(g) * u).  Every dequant warp meets the barrier once.
+      const bool go = ok && !*abort_flag;
+      const int h = (warp - 2) >> 2;
+      const int u = 4 * h + (lane >> 3);
+      const int e = u < 4 ? 2 * u : 2 * (u - 4) + 1;
+      const int cl = 8 * (8 * (q & 1) + (lane & 7)) + e;   // column among the tile's 128
+      float* xch = reinterpret_cast<float*>(sgen);
+      if (go && q >= 2) {
+#pragma unroll
+        for (int c = 0; c < NT / 16; ++c) {
+          uint32_t v[16];
+          sm100::tmem_ld_32x32b_x16(tmem + ((uint32_t)(32 * q) << 16) + kTsDCol + h * NT + c * 16, v);
+          sm100::tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) xch[(c * 16 + j) * 128 + cl] = __uint_as_float(v[j]);
+        }
+      }
+      epi_bar_sync();
+      if (go && q < 2) {
+        __half* dst = args.out + (int64_t)tile_n * (BN / 2) + cl;
+#pragma unroll
+        for (int c = 0; c < NT / 16; ++c) {
+          uint32_t v[16];
+          sm100::tmem_ld_32x32b_x16(tmem + ((uint32_t)(32 * q) << 16) + kTsDCol + h * NT + c * 16, v);
+          sm100::tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int row = tile_m * NT + c * 16 + j;
+            if (row < args.M)
+              dst[(int64_t)row * args.ldo] = __float2half_rn(
+                  silu_mul_rounded(__uint_as_float(v[j]), xch[(c * 16 + j) * 128 + cl]));
+          }
+        }
+      }
+    } else if (ok && !*abort_flag) {
       const int h = (warp - 2) >> 2;
       const int u = 4 * h + (lane >> 3);
       const int e = u < 4 ? 2 * u : 2 * (u - 4) + 1;
@@ -1196,14 +1270,18 @@ cudaError_t launch_gemm_ts(const void* x, int64_t ldx, const int32_t* qweight,
                            const int32_t* qzeros, const void* scales, void* out, int64_t ldo,
                            int M, int N, int K, int group_size, int num_sms, int* dev_status,
                            cudaStream_t stream, const char** why, const void* bias,
-                           void* workspace, size_t workspace_bytes) {
+                           void* workspace, size_t workspace_bytes, bool silu) {
   *why = nullptr;
   if (!ts_supported(x, ldx, qweight, qzeros, scales, M, N, K, group_size)) {
     *why = "shape or alignment not supported";
     return cudaSuccess;
   }
-  if (ldo < N) {
-    *why = "ldo must be at least N";
+  if (silu && (N % (2 * BN) || bias || ts_splits(M, N, K, num_sms) != 1)) {
+    *why = "SiLU-mul epilogue needs N a multiple of 512, no bias and no K split";
+    return cudaSuccess;
+  }
+  if (ldo < (silu ? N / 2 : N)) {
+    *why = silu ? "ldo must be at least N / 2" : "ldo must be at least N";
     return cudaSuccess;
   }
   const int nt = ts_tokens(M);
@@ -1212,11 +1290,12 @@ cudaError_t launch_gemm_ts(const void* x, int64_t ldx, const int32_t* qweight,
   bool ok = make_map_2d(&tmX, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, x, K, M, (uint64_t)ldx * 2, BK, nt,
                         CU_TENSOR_MAP_SWIZZLE_128B) &&
             make_map_2d(&tmW, CU_TENSOR_MAP_DATA_TYPE_INT32, qweight, N / 8, K, (uint64_t)N / 2,
-                        BN / 8, BK, CU_TENSOR_MAP_SWIZZLE_128B) &&
-            make_map_2d(&tmS, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, scales, N, G, (uint64_t)N * 2, BN, 1,
-                        CU_TENSOR_MAP_SWIZZLE_NONE) &&
+                        silu ? BN / 16 : BN / 8, BK,
+                        silu ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B) &&
+            make_map_2d(&tmS, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, scales, N, G, (uint64_t)N * 2,
+                        silu ? BN / 2 : BN, 1, CU_TENSOR_MAP_SWIZZLE_NONE) &&
             make_map_2d(&tmZ, CU_TENSOR_MAP_DATA_TYPE_INT32, qzeros, N / 8, G, (uint64_t)N / 2,
-                        BN / 8, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
+                        silu ? BN / 16 : BN / 8, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (!ok) {
     *why = "cuTensorMapEncodeTiled failed";
     return cudaSuccess;
@@ -1243,6 +1322,7 @@ cudaError_t launch_gemm_ts(const void* x, int64_t ldx, const int32_t* qweight,
   a.bias = static_cast<const __half*>(bias);
   a.splits = ts_splits(M, N, K, num_sms);
   a.part = nullptr;
+  a.silu = silu ? 1 : 0;
   if (a.splits > 1) {
     if (workspace && al16(workspace) && workspace_bytes >= ts_workspace_bytes(M, N, K, num_sms))
       a.part = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterRegionBytes);

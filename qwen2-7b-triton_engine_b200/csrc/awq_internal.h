@@ -152,13 +152,16 @@ size_t tc_workspace_bytes(int64_t M, int64_t N, int64_t K, int num_sms);
 
 // ---- small-M GEMM on tcgen05 with the dequantized weights in TMEM (awq_gemm_tc.cu) ----
 // M <= 64; same shape rules as the prefill kernel.  Tokens per CTA: 16, 32 or 64.
+// silu: gate+up product with the SiLU-mul epilogue (out [M, N/2]; N a multiple of 512,
+// no bias, only where the kernel runs without a K split).
 bool ts_supported(const void* x, int64_t ldx, const int32_t* qweight, const int32_t* qzeros,
                   const void* scales, int64_t M, int64_t N, int64_t K, int64_t group_size);
 cudaError_t launch_gemm_ts(const void* x, int64_t ldx, const int32_t* qweight,
                            const int32_t* qzeros, const void* scales, void* out, int64_t ldo,
                            int M, int N, int K, int group_size, int num_sms, int* dev_status,
                            cudaStream_t stream, const char** why, const void* bias = nullptr,
-                           void* workspace = nullptr, size_t workspace_bytes = 0);
+                           void* workspace = nullptr, size_t workspace_bytes = 0,
+                           bool silu = false);
 int ts_tokens(int64_t M);
 int ts_splits(int64_t M, int64_t N, int64_t K, int num_sms);
 size_t ts_workspace_bytes(int64_t M, int64_t N, int64_t K, int num_sms);

@@ -50,7 +50,7 @@ def test_silu_mul_vs_oracle_and_sequence(cuda, M, K, N):
     assert awq_b200.device_status() == 0
 
 
-@pytest.mark.parametrize("M", [1, 8])
+@pytest.mark.parametrize("M", [1, 8, 12, 16])
 def test_silu_mul_qwen2_gate_up(cuda, M):
     """The real MLP shape (gate+up 3584 x 37888): 74 gate / up strip pairs; repeated calls
     give the same bits (the pair counters are reset), and the product calls that share the
@@ -140,6 +140,31 @@ def test_silu_mul_tcgen05_epilogue(cuda, M, K, N):
     import awq_b200
     qw, qz, s = O.make_awq_layer(K, N, 128, seed=M + 3)
     x = O.make_x(M, K, seed=K + 5)
+    dx, dqw, dqz, ds = _dev(cuda, x, qw, qz, s)
+    a = awq_b200.gemm_silu_mul(dx, dqw, dqz, ds, 128)
+    b = awq_b200.gemm_silu_mul(dx, dqw, dqz, ds, 128)
+    torch.cuda.synchronize()
+    assert a.shape == (M, N // 2)
+    assert torch.equal(a, b)
+    assert O.max_rel_err(a.float().cpu().numpy(), O.awq_silu_mul_f32(x, qw, qz, s, 128)) <= TOL
+    seq = _sequence(awq_b200, dx, dqw, dqz, ds, 128)
+    assert O.max_rel_err(a.float().cpu().numpy(), seq.float().cpu().numpy()) <= TOL_SEQ
+    assert awq_b200.device_status() == 0
+
+
+@pytest.mark.parametrize("M,K,N", [
+    (9, 512, 37888),        # 148 CTAs of 16 tokens x (128 gate + 128 up) columns
+    (13, 256, 18944),       # 74 CTAs: the fewest that still run without a K split
+    (16, 1024, 20480),      # 80 CTAs, full 16-token tile
+])
+def test_silu_mul_small_m_tcgen05_epilogue(cuda, M, K, N):
+    """From 9 to 16 tokens the small-M tcgen05 kernel applies the SiLU-mul in its
+    epilogue when it runs without a K split (the up lanes hand their sums to the gate
+    lanes through shared memory): against the CPU oracle, the reference MLP's sequence
+    on this library's product, and bit-equal on a repeated call."""
+    import awq_b200
+    qw, qz, s = O.make_awq_layer(K, N, 128, seed=M + 7)
+    x = O.make_x(M, K, seed=K + 9)
     dx, dqw, dqz, ds = _dev(cuda, x, qw, qz, s)
     a = awq_b200.gemm_silu_mul(dx, dqw, dqz, ds, 128)
     b = awq_b200.gemm_silu_mul(dx, dqw, dqz, ds, 128)
