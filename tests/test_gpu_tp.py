@@ -104,7 +104,7 @@ def _worker(rank, world, port, M, seed, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("M", [1, 512])
+@pytest.mark.parametrize("M", [1, 12, 512])   # decode, small-M tcgen05, prefill kernels
 def test_tp_world2_matches_single_gpu(cuda, M):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
