@@ -1245,11 +1245,13 @@ cudaError_t launch_gemm_tc(const void* x, int64_t ldx, const int32_t* qweight,
 int ts_tokens(int64_t M) { return M <= 16 ? 16 : M <= 32 ? 32 : 64; }
 
 // Split-K factor of the small-M kernel: as for the prefill kernel, but a CTA keeps at
-// least 4 K steps (its ring is deeper than that, so every copy is issued at once).
+// least 4 K steps (its ring is deeper than that, so every copy is issued at once), and
+// tiles filling exactly half the SMs split in two (the gate+up shard of a 2-way tensor
+// parallel MLP, 74 tiles: at M = 16 40.9 us unsplit, 29.7 us split).
 int ts_splits(int64_t M, int64_t N, int64_t K, int num_sms) {
   const int64_t nt = ts_tokens(M);
   const int64_t tiles = ((M + nt - 1) / nt) * ((N + BN - 1) / BN);
-  if (tiles <= 0 || 2 * tiles >= num_sms) return 1;
+  if (tiles <= 0 || 2 * tiles > num_sms) return 1;
   int64_t s = num_sms / tiles;
   if (s > K / BK / kTsMinSteps) s = K / BK / kTsMinSteps;
   if (s > 16) s = 16;

@@ -154,7 +154,7 @@ def test_silu_mul_tcgen05_epilogue(cuda, M, K, N):
 
 @pytest.mark.parametrize("M,K,N", [
     (9, 512, 37888),        # 148 CTAs of 16 tokens x (128 gate + 128 up) columns
-    (13, 256, 18944),       # 74 CTAs: the fewest that still run without a K split
+    (13, 256, 18944),       # 74 CTAs (K too short to split)
     (16, 1024, 20480),      # 80 CTAs, full 16-token tile
 ])
 def test_silu_mul_small_m_tcgen05_epilogue(cuda, M, K, N):
