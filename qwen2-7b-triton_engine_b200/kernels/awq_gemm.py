@@ -83,7 +83,9 @@ def awq_gemm_silu_mul_forward(x: torch.Tensor, qweight: torch.Tensor, qzeros: to
                               scales: torch.Tensor, group_size: int = 128) -> torch.Tensor:
     """``silu(P[..., :N/2]) * P[..., N/2:]`` for ``P = awq_gemm_forward(x, ...)`` with the
     fused gate+up weights (N = 2 * intermediate): the MLP activation of the reference
-    (``model/qwen2.py:181-194``) in one call; up to 8 tokens P is never written."""
+    (``model/qwen2.py:181-194``) in one call.  The decode, small-M and prefill kernels
+    apply it in their epilogues where the shape allows (every Qwen2-7B gate+up call on one
+    GPU), and P is then never written."""
     if awq_b200._ext is not None:
         return awq_b200._ext.forward_silu_mul(x, qweight, qzeros, scales, int(group_size))
     if not isinstance(x, torch.Tensor):
