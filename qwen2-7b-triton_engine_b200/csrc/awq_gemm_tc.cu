@@ -667,7 +667,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 //               columns of k pairs); warp w owns lane quarter q = w % 4 and K blocks
 //               {2r, 2r+1} of the step, r = (w - 2) / 4
 //   warp 1      MMA: per step 2 halves x 4 K blocks of tcgen05.mma (M = 128, N = NT,
-//               K = 16, A from TMEM, B = x from shared memory), commits free both rings
+//               K = 16, A from TMEM, B = x from shared memory); one commit per step
+//               frees both rings
 //   epilogue    tcgen05.ld 32x32b: thread = one output column, NT tokens
 //
 // What bounds it (measured on B200): a tcgen05.mma of this shape costs ~30 ns however
@@ -702,7 +703,7 @@ struct TsGeo {
   static constexpr uint32_t TX_BYTES = X_BYTES + RAW_BYTES + SC_BYTES + ZR_BYTES;
   static constexpr int TSTAGES = (200 * 1024) / T_STAGE < 16 ? (200 * 1024) / T_STAGE : 16;
   static constexpr uint32_t OFF_BAR = TSTAGES * T_STAGE;
-  static constexpr uint32_t NBARS = 2 * TSTAGES + 2 * kTsAStages + 1;
+  static constexpr uint32_t NBARS = 2 * TSTAGES + kTsAStages + 1;   // tfull, tempty, afull, accf
   static constexpr uint32_t OFF_MISC = OFF_BAR + NBARS * 8;
   static constexpr uint32_t SMEM_BYTES = OFF_MISC + 16 + 1024;
   static_assert(X_BYTES % 1024 == 0, "x tile must keep the weight tile 1 KB aligned");
@@ -712,6 +713,7 @@ struct TsGeo {
                 "SiLU-mul half boxes");
   static_assert(NT * 128 * 4 <= TSTAGES * T_STAGE, "SiLU-mul epilogue exchange");
   static_assert(kTsDCol + 2 * NT <= kTsTmemCols, "TMEM columns");
+  static_assert(TSTAGES >= kTsAStages, "the copy-stage barriers also free the TMEM A stages");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
 };
 
@@ -740,8 +742,7 @@ gemm_ts_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
   auto bar_tfull = [&](int s) { return sbase + OFF_BAR + 8u * s; };
   auto bar_tempty = [&](int s) { return sbase + OFF_BAR + 8u * (TSTAGES + s); };
   auto bar_afull = [&](int s) { return sbase + OFF_BAR + 8u * (2 * TSTAGES + s); };
-  auto bar_aempty = [&](int s) { return sbase + OFF_BAR + 8u * (2 * TSTAGES + ASTAGES + s); };
-  const uint32_t bar_accf = sbase + OFF_BAR + 8u * (2 * TSTAGES + 2 * ASTAGES);
+  const uint32_t bar_accf = sbase + OFF_BAR + 8u * (2 * TSTAGES + ASTAGES);
   volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(sgen + OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sgen + OFF_MISC + 4);
 
@@ -750,10 +751,7 @@ gemm_ts_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
       sm100::mbar_init(bar_tfull(s), 1);
       sm100::mbar_init(bar_tempty(s), 1);
     }
-    for (int s = 0; s < ASTAGES; ++s) {
-      sm100::mbar_init(bar_afull(s), kDeqWarps);
-      sm100::mbar_init(bar_aempty(s), 1);
-    }
+    for (int s = 0; s < ASTAGES; ++s) sm100::mbar_init(bar_afull(s), kDeqWarps);
     sm100::mbar_init(bar_accf, 1);
     sm100::fence_mbar_init();
     *abort_flag = 0;
@@ -827,8 +825,8 @@ gemm_ts_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
             sm100::umma_f16_ts(tmem + kTsDCol + h * NT, tmem + as * 64 + h * 32 + kk * 8, bd,
                                kIdescTs, (kt | kk) != 0);
         }
+        // one commit frees both the copy stage and the TMEM A stage of this step
         sm100::umma_commit(bar_tempty(ts));
-        sm100::umma_commit(bar_aempty(as));
       }
       sm100::umma_commit(bar_accf);
     }
@@ -866,10 +864,16 @@ gemm_ts_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ 
         *abort_flag = 1;
         break;
       }
-      if (kt >= ASTAGES &&
-          !sm100::mbar_wait_bounded(bar_aempty(as), ((kt / ASTAGES) & 1) ^ 1, args.status)) {
-        *abort_flag = 1;
-        break;
+      // TMEM A stage `as` is free once the MMAs of step j = kt - ASTAGES have completed,
+      // which the copy-stage barrier of step j records (phase j / TSTAGES of slot
+      // j % TSTAGES; TSTAGES >= ASTAGES, and that slot cannot complete step j + TSTAGES
+      // before this warp has dequantized step kt, so the parity cannot alias)
+      if (kt >= ASTAGES) {
+        const int j = kt - ASTAGES;
+        if (!sm100::mbar_wait_bounded(bar_tempty(j % TSTAGES), (j / TSTAGES) & 1, args.status)) {
+          *abort_flag = 1;
+          break;
+        }
       }
       if (*abort_flag) break;
       sm100::tc_fence_after();
