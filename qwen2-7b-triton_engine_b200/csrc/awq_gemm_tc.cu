@@ -168,6 +168,37 @@ __device__ __forceinline__ void store_rows_staged(uint32_t stage, const uint32_t
   __syncwarp();
 }
 
+// As store_rows_staged for 64 columns, so that each row segment a global store writes is
+// one whole 128-byte line (col a multiple of 64 for that): stage_chunk64 writes this
+// lane's row of 32-column chunk `part` (0 or 1) into 4 KB of shared memory at `stage`,
+// flush_rows64 then writes the warp's 32 rows x 64 columns (columns at or past N, a
+// multiple of 32, and rows at or past M are not stored).  The 16-byte chunks of a row are
+// XOR-swizzled by row % 8, which keeps the row-wise writes and the chunk-wise reads free
+// of bank conflicts.
+__device__ __forceinline__ void stage_chunk64(uint32_t stage, const uint32_t (&h)[16], int part,
+                                              int lane) {
+  const uint32_t sw = (uint32_t)lane & 7u;
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    sm100::st_shared_v4(stage + (uint32_t)lane * 128u + (((uint32_t)(4 * part + j) ^ sw) << 4),
+                        h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
+}
+__device__ __forceinline__ void flush_rows64(uint32_t stage, __half* out, int64_t ldo, int row0,
+                                             int col, int M, int N, int lane) {
+  __syncwarp();
+  const int ch = lane & 7;
+  const bool col_ok = col + ch * 8 < N;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = i * 4 + (lane >> 3);
+    const uint4 v = sm100::ld_shared_v4(stage + (uint32_t)r * 128u +
+                                        (((uint32_t)ch ^ ((uint32_t)r & 7u)) << 4));
+    if (col_ok && row0 + r < M)
+      *reinterpret_cast<uint4*>(out + (int64_t)(row0 + r) * ldo + col + ch * 8) = v;
+  }
+  __syncwarp();
+}
+
 __device__ __forceinline__ void epi_bar_sync() {       // the 8 dequant / epilogue warps
   asm volatile("bar.sync 1, %0;" ::"n"(kDeqWarps * 32) : "memory");
 }
@@ -477,15 +508,18 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       const int tile = sg.tile_m * args.tiles_n + sg.tile_n;
       float* slot = shared_tile ? args.sk_part + ((size_t)tile * kSkSlots + sg.idx) * BM * BN
                                 : nullptr;
-      // fp16 results leave through 2 KB of shared memory per warp in B stage 0: every MMA
+      // fp16 results leave through 4 KB of shared memory per warp in B stage 0: every MMA
       // of this CTA so far has completed (the accumulator barrier), so no MMA reads it
-      const uint32_t stage = sbase + OFF_B + (uint32_t)dw * 2048u;
+      static_assert(kDeqWarps * 4096 <= B_BYTES, "epilogue staging fits in one B stage");
+      const uint32_t stage = sbase + OFF_B + (uint32_t)dw * 4096u;
       const int row0 = sg.tile_m * BM + acc * 128 + q * 32;
       const bool live = ok && !*abort_flag;
       if (!shared_tile && args.silu) {
         // gate chunk cg (TMEM columns 32 cg) with up chunk cg + 4 (columns 128 + 32 cg):
         // NACC == 2: chunks 0..3 of this warp's accumulator; NACC == 1: the warp's half
         const int g_lo = NACC == 2 ? 0 : half * 2, g_hi = NACC == 2 ? 4 : half * 2 + 2;
+        // one 32-column chunk per store (pairing two chunks per 128-byte line, as the plain
+        // output does, made this path slower: gate+up at M = 2048 443 us against 424)
         if (live) {
 #pragma unroll 1
           for (int cg = g_lo; cg < g_hi; ++cg) {
@@ -501,6 +535,34 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                   silu_mul_rounded(__uint_as_float(vg[2 * jj]), __uint_as_float(vu[2 * jj])),
                   silu_mul_rounded(__uint_as_float(vg[2 * jj + 1]), __uint_as_float(vu[2 * jj + 1]))));
             store_rows_staged(stage, h, args.out, args.ldo, row0, col, args.M, lane);
+          }
+        }
+      } else if (!shared_tile && args.splits == 1) {
+        // fp16 output, two 32-column chunks per store (whole 128-byte lines per row; the
+        // chunk count, 8 or 4, is even)
+        if (live) {
+#pragma unroll 1
+          for (int c = c_lo; c < c_hi; c += 2) {
+            const int col = sg.tile_n * BN + c * 32;
+            if (col >= args.N) continue;         // the same for the whole warp
+#pragma unroll 1
+            for (int part = 0; part < 2; ++part) {
+              uint32_t v[32];
+              sm100::tmem_ld_32x32b_x32(taddr + (c + part) * 32, v);
+              sm100::tmem_ld_wait();
+              const int ccol = col + part * 32;
+              if (args.bias && ccol < args.N) {  // the columns' bias, added in fp32
+#pragma unroll
+                for (int jj = 0; jj < 32; ++jj)
+                  v[jj] = __float_as_uint(__uint_as_float(v[jj]) + __half2float(args.bias[ccol + jj]));
+              }
+              uint32_t h[16];
+#pragma unroll
+              for (int jj = 0; jj < 16; ++jj)
+                h[jj] = h2_as_u32(__floats2half2_rn(__uint_as_float(v[2 * jj]), __uint_as_float(v[2 * jj + 1])));
+              stage_chunk64(stage, h, part, lane);
+            }
+            flush_rows64(stage, args.out, args.ldo, row0, col, args.M, args.N, lane);
           }
         }
       } else if (!shared_tile) {
