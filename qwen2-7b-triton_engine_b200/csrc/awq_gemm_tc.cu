@@ -440,9 +440,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const int w = lane;                      // packed word column within the tile
     const uint32_t bst_lane = (uint32_t)(w >> 3) * B_LBO + (uint32_t)dw * B_SBO;
     int j = 0;
+    int pre = 0;                             // steps of this segment dequantized already
     for (int si = 0; si < nseg; ++si) {
       const TcSeg sg = seg_at(si);
-      for (int kt = sg.k0; kt < sg.k1; ++kt, ++j) {
+      // The next segment's first step is dequantized before this segment's epilogue, so
+      // that its MMAs can start as soon as the epilogue has read the accumulator (the
+      // step body depends on the global step j only).
+      const int extra = (si + 1 < nseg && seg_at(si + 1).k1 > seg_at(si + 1).k0) ? 1 : 0;
+      for (int t = pre; t < (sg.k1 - sg.k0) + extra; ++t, ++j) {
         const int rs = j % RSTAGES, bs = j % BSTAGES;
         // The packed tile is dequantized into registers as soon as it lands and its weight
         // stage is released at once; only the shared-memory stores wait for the B stage
@@ -489,6 +494,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         __syncwarp();
         if (lane == 0) sm100::mbar_arrive(bar_bfull(bs));
       }
+      pre = extra;
 
       // ----------------------------------------------------------- epilogue --------
       // the segment's accumulator: phase si of the accumulator barrier
@@ -508,10 +514,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       const int tile = sg.tile_m * args.tiles_n + sg.tile_n;
       float* slot = shared_tile ? args.sk_part + ((size_t)tile * kSkSlots + sg.idx) * BM * BN
                                 : nullptr;
-      // fp16 results leave through 4 KB of shared memory per warp in B stage 0: every MMA
-      // of this CTA so far has completed (the accumulator barrier), so no MMA reads it
+      // fp16 results leave through 4 KB of shared memory per warp in B stage j % BSTAGES:
+      // every MMA of this segment has completed (the accumulator barrier), and the stage
+      // that holds the next segment's first step, if any, is (j - 1) % BSTAGES
       static_assert(kDeqWarps * 4096 <= B_BYTES, "epilogue staging fits in one B stage");
-      const uint32_t stage = sbase + OFF_B + (uint32_t)dw * 4096u;
+      const uint32_t stage = sbase + OFF_B + (uint32_t)(j % BSTAGES) * B_BYTES + (uint32_t)dw * 4096u;
       const int row0 = sg.tile_m * BM + acc * 128 + q * 32;
       const bool live = ok && !*abort_flag;
       if (!shared_tile && args.silu) {
@@ -690,8 +697,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           if (dw == 0 && lane == 0) args.sk_cnt[tile] = 0;   // ready for the next call
         }
       }
-      // every epilogue thread has read the accumulator and left the staging area (B stage
-      // 0, which the next segment's dequant writes)
+      // every epilogue thread has read the accumulator and left the staging area (the B
+      // stage that the next segment's second step is dequantized into)
       sm100::tc_fence_before();
       epi_bar_sync();
       if (si + 1 < nseg && dw == 0 && lane == 0) sm100::mbar_arrive(bar_tmem_empty);
