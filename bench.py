@@ -722,7 +722,7 @@ def mlp_block_bench(torch, awq_b200, dev, world, rank, comm):
     for M in (1, 16, 512):
         x = torch.randn((M, HIDDEN), device=dev, generator=gen).half()
         graph = M <= 16                    # decode: replayed from a CUDA graph
-        ms = _dev_time_ms(torch, dev, world, lambda: mlp(x), 20 if graph else 5, graph)
+        ms = _dev_time_ms(torch, dev, world, lambda: mlp(x), 20, graph)
         h = torch.randn((M, mlp.inter_local), device=dev, generator=gen).half()
         prod_ms = _dev_time_ms(torch, dev, world, lambda: awq_b200.gemm(h, w.qweight, w.qzeros,
                                                                        w.scales, GS), 20, graph)
