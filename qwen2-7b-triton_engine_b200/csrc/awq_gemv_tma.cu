@@ -797,7 +797,9 @@ cudaError_t launch_gemv_tma(const GemvTmaPlan& p, const void* x, int64_t ldx,
   cuuint32_t estr[2] = {1, 1};
   if (enc(&tm, CU_TENSOR_MAP_DATA_TYPE_INT32, 2, const_cast<int32_t*>(qweight), dims, strides, box,
           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+          // 128-byte promotion, the size of one box row: 256 bytes measured 0.4 % slower
+          // over the decode stack (1.1017 against 1.0976 ms per step)
+          CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return cudaErrorInvalidValue;
   TmaGemvArgs a;
   a.x = static_cast<const __half*>(x);
