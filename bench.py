@@ -70,8 +70,8 @@ SWEEP = {"q_o": (HIDDEN, HIDDEN), "k_v": (HIDDEN, 512), "qkv": (HIDDEN, 4608),
 # stack shape, from `ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum` (summary and
 # command in profiles/gemv_tma_decode_traffic.md).  Per launch of the stack this averages
 # to within 1 % of the algorithmic bytes: no re-reads.
-NCU_TRAFFIC_M1 = {"qkv": 8638976, "o": 6732544, "gate_up": 70607360 + 587264,
-                  "down": 35363328}
+NCU_TRAFFIC_M1 = {"qkv": 8639232, "o": 6732544, "gate_up": 70606592 + 321024,
+                  "down": 35363840}
 
 
 def alg_bytes(M, K, N, gs=GS):
